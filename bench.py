@@ -1,0 +1,453 @@
+"""Benchmark: TFLOP/s and fraction of B200 tensor peak for the reference's kernels.
+
+    python bench.py [--gpus N --steps K --warmup W] [--config C4] [--impl ours|reference] [--no-suite]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 \
+        --master-port P bench.py --gpus N --steps K --warmup W
+
+One step = one pass of the hot path over one batch of synthetic input. The headline workload
+is C4 (matmul, bf16 in / fp32 out, 8192^3), sharded by contiguous row blocks of M across ranks
+(total work fixed: strong scaling; no collective on the data path). Rank 0 prints ONE JSON line.
+
+Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events on the launch
+stream, with a 256 MiB L2 flush (torch fill) between steps outside the events; barrier +
+synchronize around the timed loop; the max over ranks of the summed step time is the job time.
+`e2e` repeats the metric through the reference-facing slot ABI (kg_sm100_matmul_entry) with
+pinned HOST buffers: H2D of the step's inputs, the kernel, D2H of the result, every step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "TFLOP/s and % of B200 tensor peak for matmul/conv2d/flash-attn at 1/2/4/8 GPU"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="C4", choices=["C1", "C2", "C3", "C4", "C5"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-suite", action="store_true", help="skip the other configurations")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    return ap.parse_args(argv)
+
+
+def load_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {k: float(data[k]) for k in FALLBACK_PEAKS if k in data}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic(kernel: str, config: str):
+    """DRAM bytes per launch of `kernel` on `config` from the committed ncu summary, or None."""
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    data = json.loads(path.read_text())
+    entry = data.get(f"{kernel}/{config}")
+    return None if entry is None else entry.get("dram_bytes_per_launch")
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            out_dir = ROOT / "gpurun_out"
+            out_dir.mkdir(exist_ok=True)
+            self.path = out_dir / f"clocks_rank{os.environ.get('RANK', '0')}.csv"
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms",
+                                          "100", "-i", str(self.device_index)], stdout=self.fh, stderr=subprocess.DEVNULL)
+            time.sleep(0.25)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or self.path is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names[1:], parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": sorted(reasons)}
+        loaded = [x for x in sm if x > 0.5 * max(sm)] or sm
+        return {"sm_mhz": float(np.median(loaded)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- distributed plumbing
+def init_dist():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def reduce_max(value: float, world: int) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum(value: float, world: int) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- workloads on the device
+def to_device(x, dev):
+    import torch
+
+    if x.dtype == np.uint16:
+        return torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(dev)
+    return torch.from_numpy(x).to(dev)
+
+
+def shard_range(total: int, rank: int, world: int):
+    return total * rank // world, total * (rank + 1) // world
+
+
+class Workload:
+    """Device buffers plus a `step()` that launches the hot path once on `stream`."""
+
+    def __init__(self, cfg, rank, world, dev):
+        import torch
+
+        from kernelcode_generate_b200 import kernels
+
+        self.cfg = cfg
+        self.kernels = kernels
+        inp = __import__("kernelcode_generate_b200.workloads", fromlist=["make_inputs"]).make_inputs(cfg)
+        s = cfg.shape
+        self.host = inp
+        if cfg.kernel == "matmul":
+            r0, r1 = shard_range(s["M"], rank, world)
+            self.rows = (r0, r1)
+            self.lhs_host = np.ascontiguousarray(inp["lhs"][r0:r1])
+            self.lhs = to_device(self.lhs_host, dev)
+            self.rhs = to_device(inp["rhs"], dev)
+            self.out = torch.empty(r1 - r0, s["N"], device=dev)
+            self.flops = 2 * (r1 - r0) * s["N"] * s["K"]
+            self.kernel_name = "gemm_bf16_tc_kernel" if cfg.dtype == "bf16" else "matmul_simt_kernel<f32>"
+        elif cfg.kernel == "flash_attention":
+            bh = s["B"] * s["H"]
+            b0, b1 = shard_range(bh, rank, world)
+            self.rows = (b0, b1)
+            shape = (1, b1 - b0, s["S"], s["D"])
+            self.q, self.k, self.v = (to_device(np.ascontiguousarray(inp[n].reshape(bh, s["S"], s["D"])[b0:b1]).reshape(shape), dev)
+                                      for n in ("q", "k", "v"))
+            self.out = torch.empty_like(self.q)
+            full = 4 * s["S"] * s["S"] * s["D"] * (b1 - b0)
+            self.flops = full // 2 if s["causal"] else full
+            self.kernel_name = None
+        else:  # conv2d: batch 1, one replica per rank
+            self.x = to_device(inp["input"], dev)
+            self.w = to_device(inp["weight"], dev)
+            HO = (s["XH"] + s["pads"][0] + s["pads"][1] - s["dilation"][0] * (s["KH"] - 1) - 1) // s["stride"][0] + 1
+            WO = (s["XW"] + s["pads"][2] + s["pads"][3] - s["dilation"][1] * (s["KW"] - 1) - 1) // s["stride"][1] + 1
+            self.out = torch.empty(s["B"], s["F"], HO, WO, device=dev)
+            self.flops = cfg.flops
+            self.kernel_name = "conv2d_simt_kernel<f32>"
+
+    def step(self, stream):
+        c, s = self.cfg, self.cfg.shape
+        if c.kernel == "matmul":
+            self.kernels.matmul(self.out, self.lhs, self.rhs, None, stream=stream)
+        elif c.kernel == "flash_attention":
+            self.kernels.flash_attention(self.out, self.q, self.k, self.v, s["scale"], s["causal"], stream=stream)
+        else:
+            self.kernels.conv2d(self.out, self.x, self.w, None, s["stride"], s["dilation"], s["pads"], stream=stream)
+
+
+def time_steps(wl, steps, warmup, world, flush):
+    """Returns (max-over-ranks summed step ms, per-launch mean ms, kernel name)."""
+    import torch
+
+    from kernelcode_generate_b200 import runtime
+
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        wl.step(stream)
+    torch.cuda.synchronize()
+    kernel = runtime.last_kernel()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    barrier(world)
+    for i in range(steps):
+        if flush is not None:
+            flush.fill_(i & 0xFF)  # evict L2 (256 MiB write), outside the timed events
+        starts[i].record(stream)
+        wl.step(stream)
+        ends[i].record(stream)
+    barrier(world)
+    total = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    if runtime.device_status() != 0:
+        raise RuntimeError("a kernel reported a pipeline timeout during the timed region")
+    return reduce_max(total, world), total / steps, kernel
+
+
+def e2e_matmul(cfg, wl, steps, world):
+    """Metric through the slot ABI with pinned host buffers (H2D + kernel + D2H per step)."""
+    import torch
+
+    from kernelcode_generate_b200 import kernels
+
+    s = cfg.shape
+    lhs = torch.from_numpy(wl.lhs_host.view(np.int16)).view(torch.bfloat16).pin_memory()
+    rhs = torch.from_numpy(wl.host["rhs"].view(np.int16)).view(torch.bfloat16).pin_memory()
+    out = torch.empty(wl.out.shape, dtype=torch.float32).pin_memory()
+    tiles = cfg.tiles
+    kernels.matmul_inputs_dynamic_tile_dynamic_kernel(out, lhs, rhs, None, *tiles)  # warm-up (staging arena)
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        kernels.matmul_inputs_dynamic_tile_dynamic_kernel(out, lhs, rhs, None, *tiles)
+    barrier(world)
+    elapsed = reduce_max(time.perf_counter() - t0, world)
+    total_flops = 2 * s["M"] * s["N"] * s["K"]
+    h2d = lhs.numel() * 2 + rhs.numel() * 2
+    d2h = out.numel() * 4
+    return {"value": round(total_flops * steps / elapsed / 1e12, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "ms_per_step": round(elapsed / steps * 1e3, 3),
+            "path": "kg_sm100_matmul_entry (slot ABI), pinned host buffers"}
+
+
+# ---------------------------------------------------------------- CPU reference / baseline
+def cpu_sample(cfg, threads, budget_rows=None):
+    """Runs the reference's CPU path (oracle/_ref, -O2) or the C port on a bounded sample of the
+    workload. Returns (TFLOP/s, seconds, kind, sample description)."""
+    sys.path.insert(0, str(ROOT))
+    import oracle
+
+    kind = "reference" if oracle.ref_available("O2") else "port"
+    impl = "ref" if kind == "reference" else "port"
+    inp = __import__("kernelcode_generate_b200.workloads", fromlist=["make_inputs"]).make_inputs(cfg)
+    s = cfg.shape
+    t_threads = threads if kind == "reference" else 1
+    if cfg.kernel == "matmul":
+        tile_h = 80 if cfg.dtype == "bf16" else cfg.tiles[0]
+        tiles = (tile_h, 96, 72) if cfg.dtype == "bf16" else cfg.tiles
+        rows = min(s["M"], budget_rows or tile_h * t_threads)
+        t0 = time.perf_counter()
+        oracle.matmul(inp["lhs"], inp["rhs"], None, tiles=tiles, rows=(0, rows), impl=impl, threads=t_threads)
+        dt = time.perf_counter() - t0
+        flops = 2 * rows * s["N"] * s["K"]
+        desc = f"rows 0..{rows} of M={s['M']} (tiles {tiles}), {flops / 1e9:.1f} GFLOP"
+    elif cfg.kernel == "flash_attention":
+        S = s["S"]
+        if S > 1024:
+            q_rows = (S - 128 * max(1, t_threads), S)  # last query tiles: the most work per row
+            bh = (0, 1)
+            t0 = time.perf_counter()
+            oracle.flash_attention(inp["q"], inp["k"], inp["v"], tiles=cfg.tiles, scale=s["scale"], causal=s["causal"], bh=bh,
+                                   q_rows=q_rows, impl=impl, threads=t_threads)
+            dt = time.perf_counter() - t0
+            n = q_rows[1] - q_rows[0]
+            keys = sum((r + 1) if s["causal"] else S for r in range(q_rows[0], q_rows[1]))
+            flops = 4 * keys * s["D"]
+            desc = f"(b,h)=0, query rows {q_rows[0]}..{q_rows[1]} ({n} rows), {flops / 1e9:.1f} GFLOP"
+        else:
+            t0 = time.perf_counter()
+            oracle.flash_attention(inp["q"], inp["k"], inp["v"], tiles=cfg.tiles, scale=s["scale"], causal=s["causal"], impl=impl,
+                                   threads=t_threads)
+            dt = time.perf_counter() - t0
+            flops = cfg.flops
+            desc = "full workload"
+    else:
+        t0 = time.perf_counter()
+        oracle.conv2d(inp["input"], inp["weight"], None, stride=s["stride"], dilation=s["dilation"], pads=s["pads"], tiles=cfg.tiles,
+                      impl=impl, threads=t_threads)
+        dt = time.perf_counter() - t0
+        flops = cfg.flops
+        desc = "full workload"
+    return flops / dt / 1e12, dt, kind, desc, t_threads
+
+
+def reference_arm(args):
+    """`--impl reference`: the reference's own CPU implementation of the path on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from kernelcode_generate_b200 import workloads
+
+    cfg = workloads.CONFIGS[args.config]
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup if cfg.kernel != "matmul" or cfg.dtype != "bf16" else 0):
+        cpu_sample(cfg, threads)
+    vals, secs = [], 0.0
+    kind = desc = None
+    used = threads
+    for _ in range(max(1, min(args.steps, 3))):
+        v, dt, kind, desc, used = cpu_sample(cfg, threads)
+        vals.append(v)
+        secs += dt
+    value = float(np.median(vals))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": len(vals), "warmup": args.warmup, "ms_per_step": round(secs / len(vals) * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32" if cfg.dtype == "f32" else "f32 (bf16-rounded inputs)",
+        "data": "synthetic", "config": workload_config(cfg, args.gpus),
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": used, "kind": kind,
+                         "sample": desc + " per step; npu_demo helpers g++ -O2" if kind == "reference" else desc},
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(cfg, n_gpus):
+    sharding = {"matmul": "contiguous row blocks of M", "flash_attention": "batch x heads",
+                "conv2d": "replicas (batch 1)"}[cfg.kernel]
+    return {"workload": f"{cfg.name}: {cfg.note}", **{k: v for k, v in cfg.shape.items()}, "sharding": sharding,
+            "parallelism": f"shard{n_gpus}", "l2": "256 MiB L2 flush between timed steps (outside the events)"}
+
+
+# ---------------------------------------------------------------- main
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return reference_arm(args)
+    import torch
+
+    from kernelcode_generate_b200 import workloads
+
+    rank, world, local = init_dist()
+    dev = torch.device("cuda", local)
+    peaks, peak_src = load_peaks()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    cfg = workloads.CONFIGS[args.config]
+    wl = Workload(cfg, rank, world, dev)
+    with ClockSampler(local) as clocks:
+        job_ms, launch_ms, kernel = time_steps(wl, args.steps, args.warmup, world, flush)
+    total_flops = reduce_sum(float(wl.flops), world)  # every rank's shard
+    value = total_flops * args.steps / (job_ms * 1e-3) / 1e12
+    launch_ms_max = reduce_max(launch_ms, world)
+    achieved = wl.flops / (launch_ms * 1e-3) / 1e12  # this rank's kernel, algorithmic FLOPs per launch
+    tensor_peak = peaks["bf16_tflops"]
+    traffic = load_traffic(kernel, cfg.name)
+    e2e = e2e_matmul(cfg, wl, args.e2e_steps, world) if cfg.kernel == "matmul" and cfg.dtype == "bf16" else None
+
+    suite = {}
+    if not args.no_suite:
+        for name in ("C1", "C2", "C3", "C5"):
+            if name == cfg.name:
+                continue
+            c = workloads.CONFIGS[name]
+            w2 = Workload(c, rank, world, dev)
+            steps = max(3, min(args.steps, 10))
+            ms, per_launch, k2 = time_steps(w2, steps, max(3, args.warmup), world, flush)
+            tot = reduce_sum(float(w2.flops), world)
+            v2 = tot * steps / (ms * 1e-3) / 1e12
+            suite[name] = {"value": round(v2, 3), "unit": "TFLOP/s", "ms_per_step": round(ms / steps, 4), "kernel": k2,
+                           "frac_of_bf16_peak": round(v2 / (tensor_peak * world), 4), "workload": c.note}
+            del w2
+            torch.cuda.empty_cache()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, dt, kind, desc, used = cpu_sample(cfg, os.cpu_count() or 1)
+        cpu = {"value": round(v, 6), "unit": "TFLOP/s", "cores": used, "kind": kind,
+               "sample": f"{desc}; {dt:.1f} s" + ("; npu_demo helpers g++ -O2" if kind == "reference" else "; C port, 1 thread")}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(job_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": cfg.dtype, "data": "synthetic",
+            "config": workload_config(cfg, world),
+            "frac_of_peak": round(value / (tensor_peak * world), 4),
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": tensor_peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / tensor_peak, 4), "traffic": traffic, "kernel": kernel,
+                         "peak_source": f"{peak_src} bf16_tflops (burst)",
+                         "launch_ms": round(launch_ms, 4), "launch_ms_max_over_ranks": round(launch_ms_max, 4),
+                         "algorithmic_flop_per_launch": int(wl.flops)},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+            "suite": suite,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

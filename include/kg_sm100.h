@@ -1,0 +1,130 @@
+/*
+ * kg_sm100.h -- C ABI of the B200 (sm_100a) backend for the three kernels that
+ * violetDelia/kernelcode_generate generates and runs: tiled matmul, conv2d and flash attention.
+ *
+ * Two families of entry points:
+ *
+ *  1. Slot entries -- the reference's compiled-kernel ABI, unchanged:
+ *         int kg_execute_entry(const _ArgSlot* ordered_args, unsigned long long arg_count)
+ *     (generated shim: kernel_gen/execute_engine/builtin_strategy/common.py:925; cuda_sm89 form:
+ *     kernel_gen/dsl/gen_kernel/emit/cuda_sm89/source_bundle.py:1826; Python marshalling:
+ *     kernel_gen/execute_engine/runtime_args.py:591-664). Arguments are the DSL function's
+ *     positional parameters, out first. Memory slots may hold DEVICE pointers (torch CUDA tensors)
+ *     or HOST pointers (numpy arrays); host buffers are staged through device memory inside the
+ *     call. The call is synchronous, as the reference's is (include/cuda_sm89/Arch.h:168).
+ *     libkg_sm100_{matmul,conv2d,flash_attention}.so each export `kg_execute_entry`, forwarding
+ *     to the named entries below, so a compiled-kernel path is a drop-in.
+ *
+ *  2. Typed entries -- plain device pointers and sizes, stream-ordered, no synchronisation:
+ *     what the kernels compute, without the slot marshalling; used by bench.py and by callers
+ *     that manage their own buffers and streams.
+ *
+ * Return codes (all entries): 0 ok; KG_ERR_* otherwise. kg_sm100_last_error() gives the
+ * message of the calling thread's most recent failure. A non-zero slot-entry return is what
+ * the reference maps to "runtime_throw_or_abort: entry_point returned non-zero"
+ * (kernel_gen/execute_engine/compiler.py:342-352); unlike the reference's cuda_sm89 runtime,
+ * which aborts the process on a CUDA error (include/cuda_sm89/Arch.h:54-71), every error here
+ * is returned.
+ */
+#ifndef KG_SM100_H_
+#define KG_SM100_H_
+
+#if defined(__GNUC__)
+#define KG_API __attribute__((visibility("default")))
+#else
+#define KG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Slot layout: 64 bytes, natural alignment (offsets kind 0, data 8, shape 16, stride 24, rank 32,
+ * dtype_code 40, int_value 48, float_value 56). Mirrors _CArgSlot,
+ * kernel_gen/execute_engine/runtime_args.py:217-237. */
+typedef struct KgArgSlot {
+    int kind;                 /* 1 memory, 2 int64 scalar, 3 double scalar */
+    void* data;               /* memory: host or device pointer; NULL for an absent optional arg */
+    const long long* shape;   /* memory: `rank` extents */
+    const long long* stride;  /* memory: `rank` strides in ELEMENTS (must be contiguous row-major) */
+    unsigned long long rank;
+    int dtype_code;           /* memory: KG_DTYPE_* */
+    long long int_value;      /* kind 2 */
+    double float_value;       /* kind 3 */
+} KgArgSlot;
+
+#define KG_SLOT_MEMORY 1
+#define KG_SLOT_INT 2
+#define KG_SLOT_FLOAT 3
+
+/* dtype codes 1..4 are the reference's (runtime_args.py:94-110); 5 (bf16) is new here. */
+#define KG_DTYPE_F32 1
+#define KG_DTYPE_F64 2
+#define KG_DTYPE_I32 3
+#define KG_DTYPE_I64 4
+#define KG_DTYPE_BF16 5
+
+#define KG_OK 0
+#define KG_ERR_INVALID_ARGUMENT 1 /* bad slot count / kind / dtype / shape / stride */
+#define KG_ERR_UNSUPPORTED 2      /* valid request this backend does not implement */
+#define KG_ERR_CUDA 3             /* a CUDA runtime call failed */
+#define KG_ERR_DEVICE_TIMEOUT 4   /* a kernel gave up waiting on its own pipeline (device status word set) */
+
+/* ---------------------------------------------------------------- slot entries */
+
+/* matmul_inputs_dynamic_tile_dynamic_kernel(out[H,W] f32, lhs[H,K], rhs[K,W], bias[W] f32 | absent,
+ *                                           tile_h, tile_w, tile_k)
+ * Replaces the compiled kernel of kernel/matmul/inputs_dynamic_tile_dynamic.py:57-113 (the static
+ * variants' wrappers, inputs_static_tile_static.py:334-388 / inputs_static_tile_dynamic.py, take the
+ * same slots). lhs/rhs are both f32 or both bf16; tiles must be positive and only select nothing
+ * (the GPU uses its own tiling). 7 slots. */
+KG_API int kg_sm100_matmul_entry(const KgArgSlot* ordered_args, unsigned long long arg_count);
+
+/* conv2d_inputs_dynamic_tile_dynamic_kernel(out[B,F,HO,WO] f32, input[B,C,XH,XW], weight[F,C,KH,KW],
+ *     bias[F] f32 | absent, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_bottom,
+ *     pad_left, pad_right, tile_f, tile_c, tile_n, tile_ho, tile_wo)
+ * Replaces kernel/conv2d/inputs_dynamic_tile_dynamic.py:102-205. 17 slots. */
+KG_API int kg_sm100_conv2d_entry(const KgArgSlot* ordered_args, unsigned long long arg_count);
+
+/* flash_attention_inputs_dynamic_tile_dynamic_kernel(out, q, k, v [B,H,S,D], br, bc[, scale, causal])
+ * Replaces kernel/flash_attention/inputs_dynamic_tile_dynamic.py:96-195. With 6 slots the result is
+ * the reference's softmax(q k^T) v; two optional trailing slots (extension) give the score scale
+ * (float slot) and a causal flag (int slot). out has the dtype of q/k/v (f32 or bf16). */
+KG_API int kg_sm100_flash_attention_entry(const KgArgSlot* ordered_args, unsigned long long arg_count);
+
+/* ---------------------------------------------------------------- typed entries */
+
+/* out[M,N] (f32) = lhs[M,K] . rhs[K,N] (+ bias[N]); lhs/rhs row-major, in_dtype KG_DTYPE_F32 or
+ * KG_DTYPE_BF16 (bf16 runs on tcgen05 tensor cores, f32 on exact FFMA). stream: cudaStream_t. */
+KG_API int kg_sm100_matmul(float* out, const void* lhs, const void* rhs, int in_dtype, const float* bias,
+                    long long M, long long K, long long N, void* stream);
+
+/* NCHW conv2d: out[B,F,HO,WO] (f32) with HO = (XH+pt+pb-dh*(KH-1)-1)/sh+1, WO likewise. */
+KG_API int kg_sm100_conv2d(float* out, const void* input, const void* weight, int in_dtype, const float* bias,
+                    long long B, long long C, long long XH, long long XW, long long F, long long KH, long long KW,
+                    long long stride_h, long long stride_w, long long dilation_h, long long dilation_w,
+                    long long pad_top, long long pad_bottom, long long pad_left, long long pad_right, void* stream);
+
+/* out = softmax(q k^T * scale [causal]) v over [B,H,S,D]; out/q/k/v all `dtype`. */
+KG_API int kg_sm100_flash_attention(void* out, const void* q, const void* k, const void* v, int dtype,
+                             long long B, long long H, long long S, long long D, float scale, int causal,
+                             void* stream);
+
+/* Synchronises the current device, returns its device status word (0 = no kernel reported a
+ * pipeline timeout since the last call) in *code and clears it. */
+KG_API int kg_sm100_device_status(int* code);
+
+/* Message of the calling thread's most recent failing call ("" if none). */
+KG_API const char* kg_sm100_last_error(void);
+
+/* Name of the kernel the most recent typed call on this thread launched (for reports). */
+KG_API const char* kg_sm100_last_kernel(void);
+
+/* ABI version of this library. */
+KG_API int kg_sm100_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KG_SM100_H_ */

@@ -1,0 +1,475 @@
+// C ABI of the sm_100a backend (declared in include/kg_sm100.h): argument validation, slot
+// unmarshalling, host-buffer staging, TMA descriptor creation and kernel dispatch.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/kg_sm100.h"
+#include "kg_gemm_tc.h"
+#include "kg_simt.h"
+
+// One status word per device (module globals are per device). Kernels record pipeline timeouts here.
+__device__ int kg_device_status_word;
+
+namespace {
+
+thread_local std::string g_last_error;
+thread_local const char* g_last_kernel = "";
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(KG_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define KG_CUDA_TRY(call)                     \
+    do {                                      \
+        cudaError_t kg_e_ = (call);           \
+        if (kg_e_ != cudaSuccess) {           \
+            return cuda_fail(kg_e_, #call);   \
+        }                                     \
+    } while (0)
+
+struct DeviceInfo {
+    int num_sms = 0;
+    int* status = nullptr;  // device address of kg_device_status_word
+};
+
+std::mutex g_mu;
+std::vector<DeviceInfo> g_devices;
+// Slot entries are synchronous and share one staging arena per device: one call at a time.
+std::mutex g_call_mu;
+
+int device_info(DeviceInfo** out) {
+    int dev = 0;
+    KG_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (static_cast<int>(g_devices.size()) <= dev) {
+        g_devices.resize(dev + 1);
+    }
+    DeviceInfo& info = g_devices[dev];
+    if (info.num_sms == 0) {
+        KG_CUDA_TRY(cudaDeviceGetAttribute(&info.num_sms, cudaDevAttrMultiProcessorCount, dev));
+        void* p = nullptr;
+        KG_CUDA_TRY(cudaGetSymbolAddress(&p, kg_device_status_word));
+        info.status = static_cast<int*>(p);
+    }
+    *out = &info;
+    return KG_OK;
+}
+
+// ------------------------------------------------------------------ TMA descriptors
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                   const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encode_fn(EncodeTiledFn* fn) {
+    static EncodeTiledFn cached = nullptr;
+    static std::once_flag once;
+    static cudaError_t err = cudaSuccess;
+    std::call_once(once, []() {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) {
+            cached = reinterpret_cast<EncodeTiledFn>(p);
+        }
+    });
+    if (cached == nullptr) {
+        return fail(KG_ERR_CUDA, "cuTensorMapEncodeTiled unavailable (%s)", cudaGetErrorName(err));
+    }
+    *fn = cached;
+    return KG_OK;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix, box {box_cols, box_rows}, 128B swizzle.
+int make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, int box_cols, int box_rows) {
+    EncodeTiledFn encode = nullptr;
+    int rc = get_encode_fn(&encode);
+    if (rc != KG_OK) return rc;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+    cuuint32_t estrides[2] = {1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estrides,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        return fail(KG_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld", static_cast<int>(r), rows, cols);
+    }
+    return KG_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------------ typed implementations
+int matmul_impl(float* out, const void* lhs, const void* rhs, int in_dtype, const float* bias, long long M, long long K, long long N,
+                cudaStream_t stream) {
+    if (!out || !lhs || !rhs) return fail(KG_ERR_INVALID_ARGUMENT, "matmul: null pointer");
+    if (M <= 0 || K <= 0 || N <= 0) return fail(KG_ERR_INVALID_ARGUMENT, "matmul: sizes must be positive (M=%lld K=%lld N=%lld)", M, K, N);
+    if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL) return fail(KG_ERR_UNSUPPORTED, "matmul: sizes beyond int32");
+    DeviceInfo* dev = nullptr;
+    int rc = device_info(&dev);
+    if (rc != KG_OK) return rc;
+    if (in_dtype == KG_DTYPE_BF16) {
+        if (kg::gemm_bf16_tc_supported(M, N, K) && aligned16(lhs) && aligned16(rhs)) {
+            CUtensorMap ta, tb;
+            rc = make_tmap_2d_bf16(&ta, lhs, M, K, 64, kg::gemm_bf16_tc_tile_m());
+            if (rc != KG_OK) return rc;
+            rc = make_tmap_2d_bf16(&tb, rhs, K, N, 64, 64);
+            if (rc != KG_OK) return rc;
+            g_last_kernel = "gemm_bf16_tc_kernel";
+            KG_CUDA_TRY(kg::gemm_bf16_tc_launch(ta, tb, out, bias, (int)M, (int)N, (int)K, dev->num_sms, dev->status, stream));
+            return KG_OK;
+        }
+        g_last_kernel = "matmul_simt_kernel<bf16>";
+        KG_CUDA_TRY(kg::matmul_simt_launch(out, static_cast<const __nv_bfloat16*>(lhs), static_cast<const __nv_bfloat16*>(rhs), bias,
+                                           (int)M, (int)N, (int)K, stream));
+        return KG_OK;
+    }
+    if (in_dtype == KG_DTYPE_F32) {
+        g_last_kernel = "matmul_simt_kernel<f32>";
+        KG_CUDA_TRY(kg::matmul_simt_launch(out, static_cast<const float*>(lhs), static_cast<const float*>(rhs), bias, (int)M, (int)N,
+                                           (int)K, stream));
+        return KG_OK;
+    }
+    return fail(KG_ERR_UNSUPPORTED, "matmul: input dtype code %d not supported (f32=1, bf16=5)", in_dtype);
+}
+
+int conv2d_impl(float* out, const void* input, const void* weight, int in_dtype, const float* bias, const kg::Conv2dShape& s,
+                cudaStream_t stream) {
+    if (!out || !input || !weight) return fail(KG_ERR_INVALID_ARGUMENT, "conv2d: null pointer");
+    if (in_dtype == KG_DTYPE_F32) {
+        g_last_kernel = "conv2d_simt_kernel<f32>";
+        KG_CUDA_TRY(kg::conv2d_simt_launch(out, static_cast<const float*>(input), static_cast<const float*>(weight), bias, s, stream));
+        return KG_OK;
+    }
+    if (in_dtype == KG_DTYPE_BF16) {
+        g_last_kernel = "conv2d_simt_kernel<bf16>";
+        KG_CUDA_TRY(kg::conv2d_simt_launch(out, static_cast<const __nv_bfloat16*>(input), static_cast<const __nv_bfloat16*>(weight),
+                                           bias, s, stream));
+        return KG_OK;
+    }
+    return fail(KG_ERR_UNSUPPORTED, "conv2d: input dtype code %d not supported (f32=1, bf16=5)", in_dtype);
+}
+
+int conv2d_shape(kg::Conv2dShape* s, long long B, long long C, long long XH, long long XW, long long F, long long KH, long long KW,
+                 long long sh, long long sw, long long dh, long long dw, long long pt, long long pb, long long pl, long long pr) {
+    if (B <= 0 || C <= 0 || XH <= 0 || XW <= 0 || F <= 0 || KH <= 0 || KW <= 0)
+        return fail(KG_ERR_INVALID_ARGUMENT, "conv2d: extents must be positive");
+    if (sh <= 0 || sw <= 0 || dh <= 0 || dw <= 0) return fail(KG_ERR_INVALID_ARGUMENT, "conv2d: stride/dilation must be positive");
+    if (pt < 0 || pb < 0 || pl < 0 || pr < 0) return fail(KG_ERR_INVALID_ARGUMENT, "conv2d: padding must be non-negative");
+    const long long HO = (XH + pt + pb - dh * (KH - 1) - 1) / sh + 1;
+    const long long WO = (XW + pl + pr - dw * (KW - 1) - 1) / sw + 1;
+    if (XH + pt + pb - dh * (KH - 1) - 1 < 0 || XW + pl + pr - dw * (KW - 1) - 1 < 0 || HO <= 0 || WO <= 0)
+        return fail(KG_ERR_INVALID_ARGUMENT, "conv2d: empty output");
+    const long long lim = 0x7fffffffLL;
+    if (B * C * XH * XW > lim || F * C * KH * KW > lim || B * F * HO * WO > lim) return fail(KG_ERR_UNSUPPORTED, "conv2d: tensor beyond int32 elements");
+    *s = kg::Conv2dShape{(int)B, (int)C, (int)XH, (int)XW, (int)F, (int)KH, (int)KW, (int)HO, (int)WO,
+                         (int)sh, (int)sw, (int)dh, (int)dw, (int)pt, (int)pb, (int)pl, (int)pr};
+    return KG_OK;
+}
+
+int flash_attention_impl(void* out, const void* q, const void* k, const void* v, int dtype, long long B, long long H, long long S,
+                         long long D, float scale, int causal, cudaStream_t stream) {
+    if (!out || !q || !k || !v) return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention: null pointer");
+    if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention: extents must be positive");
+    if (B * H > 65535) return fail(KG_ERR_UNSUPPORTED, "flash_attention: B*H > 65535");
+    if (S > 0x7fffffffLL || D > 128) return fail(KG_ERR_UNSUPPORTED, "flash_attention: head dim %lld > 128 not supported", D);
+    if (!std::isfinite(scale)) return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention: scale must be finite");
+    if (dtype == KG_DTYPE_F32) {
+        g_last_kernel = "flash_attn_simt_kernel<f32>";
+        KG_CUDA_TRY(kg::flash_attn_simt_launch(static_cast<float*>(out), static_cast<const float*>(q), static_cast<const float*>(k),
+                                               static_cast<const float*>(v), (int)B, (int)H, (int)S, (int)D, scale, causal, stream));
+        return KG_OK;
+    }
+    if (dtype == KG_DTYPE_BF16) {
+        g_last_kernel = "flash_attn_simt_kernel<bf16>";
+        KG_CUDA_TRY(kg::flash_attn_simt_launch(static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(q),
+                                               static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v), (int)B,
+                                               (int)H, (int)S, (int)D, scale, causal, stream));
+        return KG_OK;
+    }
+    return fail(KG_ERR_UNSUPPORTED, "flash_attention: dtype code %d not supported (f32=1, bf16=5)", dtype);
+}
+
+// ------------------------------------------------------------------ slot marshalling
+size_t dtype_size(int code) {
+    switch (code) {
+        case KG_DTYPE_F32: return 4;
+        case KG_DTYPE_F64: return 8;
+        case KG_DTYPE_I32: return 4;
+        case KG_DTYPE_I64: return 8;
+        case KG_DTYPE_BF16: return 2;
+        default: return 0;
+    }
+}
+
+struct MemArg {
+    void* data = nullptr;       // pointer the caller passed
+    void* dev = nullptr;        // device-accessible pointer used by the kernel
+    std::vector<long long> shape;
+    int dtype = 0;
+    size_t bytes = 0;
+    bool host = false;          // caller passed host memory: staged through `dev`
+};
+
+int read_mem(const KgArgSlot* slots, unsigned long long i, const char* name, bool optional, int rank, MemArg* m) {
+    const KgArgSlot& s = slots[i];
+    if (s.kind != KG_SLOT_MEMORY) return fail(KG_ERR_INVALID_ARGUMENT, "slot %llu (%s): expected memory, got kind %d", i, name, s.kind);
+    if (s.data == nullptr) {
+        if (optional) {
+            m->data = nullptr;
+            return KG_OK;
+        }
+        return fail(KG_ERR_INVALID_ARGUMENT, "slot %llu (%s): null data", i, name);
+    }
+    if (static_cast<int>(s.rank) != rank || s.shape == nullptr || s.stride == nullptr)
+        return fail(KG_ERR_INVALID_ARGUMENT, "slot %llu (%s): expected rank %d, got %llu", i, name, rank, s.rank);
+    const size_t esz = dtype_size(s.dtype_code);
+    if (esz == 0) return fail(KG_ERR_INVALID_ARGUMENT, "slot %llu (%s): unknown dtype code %d", i, name, s.dtype_code);
+    long long expect = 1;
+    long long count = 1;
+    for (int d = rank - 1; d >= 0; --d) {
+        if (s.shape[d] <= 0) return fail(KG_ERR_INVALID_ARGUMENT, "slot %llu (%s): extent %d is %lld", i, name, d, s.shape[d]);
+        if (s.stride[d] != expect && s.shape[d] != 1)
+            return fail(KG_ERR_INVALID_ARGUMENT, "slot %llu (%s): memory arg is not contiguous", i, name);
+        expect *= s.shape[d];
+    }
+    count = expect;
+    m->data = s.data;
+    m->shape.assign(s.shape, s.shape + rank);
+    m->dtype = s.dtype_code;
+    m->bytes = static_cast<size_t>(count) * esz;
+    return KG_OK;
+}
+
+int read_int(const KgArgSlot* slots, unsigned long long i, const char* name, long long* v) {
+    if (slots[i].kind != KG_SLOT_INT) return fail(KG_ERR_INVALID_ARGUMENT, "slot %llu (%s): expected int, got kind %d", i, name, slots[i].kind);
+    *v = slots[i].int_value;
+    return KG_OK;
+}
+
+// Per-device staging arena for host-memory arguments (grow-only, reused across calls).
+struct Staging {
+    void* ptr = nullptr;
+    size_t cap = 0;
+};
+std::vector<Staging> g_staging;
+
+int stage_in(std::vector<MemArg*>& args, cudaStream_t stream) {
+    size_t total = 0;
+    for (MemArg* m : args) {
+        if (m->data == nullptr) continue;
+        cudaPointerAttributes attr;
+        cudaError_t e = cudaPointerGetAttributes(&attr, m->data);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            attr.type = cudaMemoryTypeUnregistered;
+        }
+        m->host = !(attr.type == cudaMemoryTypeDevice || attr.type == cudaMemoryTypeManaged);
+        if (m->host) total += (m->bytes + 255) & ~size_t(255);
+        else m->dev = m->data;
+    }
+    if (total == 0) return KG_OK;
+    int dev = 0;
+    KG_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (static_cast<int>(g_staging.size()) <= dev) g_staging.resize(dev + 1);
+    Staging& st = g_staging[dev];
+    if (st.cap < total) {
+        if (st.ptr) KG_CUDA_TRY(cudaFree(st.ptr));
+        st.ptr = nullptr;
+        st.cap = 0;
+        KG_CUDA_TRY(cudaMalloc(&st.ptr, total));
+        st.cap = total;
+    }
+    size_t off = 0;
+    for (MemArg* m : args) {
+        if (m->data == nullptr || !m->host) continue;
+        m->dev = static_cast<char*>(st.ptr) + off;
+        off += (m->bytes + 255) & ~size_t(255);
+        KG_CUDA_TRY(cudaMemcpyAsync(m->dev, m->data, m->bytes, cudaMemcpyHostToDevice, stream));
+    }
+    return KG_OK;
+}
+
+int finish_call(int rc, MemArg* out, cudaStream_t stream) {
+    if (rc != KG_OK) {
+        cudaStreamSynchronize(stream);
+        return rc;
+    }
+    if (out->host) KG_CUDA_TRY(cudaMemcpyAsync(out->data, out->dev, out->bytes, cudaMemcpyDeviceToHost, stream));
+    KG_CUDA_TRY(cudaStreamSynchronize(stream));
+    DeviceInfo* dev = nullptr;
+    rc = device_info(&dev);
+    if (rc != KG_OK) return rc;
+    int code = 0;
+    KG_CUDA_TRY(cudaMemcpy(&code, dev->status, sizeof(int), cudaMemcpyDeviceToHost));
+    if (code != 0) {
+        const int zero = 0;
+        cudaMemcpy(dev->status, &zero, sizeof(int), cudaMemcpyHostToDevice);
+        return fail(KG_ERR_DEVICE_TIMEOUT, "kernel %s reported device status %d (pipeline wait timed out)", g_last_kernel, code);
+    }
+    return KG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kg_sm100_abi_version(void) { return 1; }
+
+const char* kg_sm100_last_error(void) { return g_last_error.c_str(); }
+
+const char* kg_sm100_last_kernel(void) { return g_last_kernel; }
+
+int kg_sm100_device_status(int* code) {
+    if (code == nullptr) return fail(KG_ERR_INVALID_ARGUMENT, "device_status: null code");
+    DeviceInfo* dev = nullptr;
+    int rc = device_info(&dev);
+    if (rc != KG_OK) return rc;
+    KG_CUDA_TRY(cudaDeviceSynchronize());
+    KG_CUDA_TRY(cudaMemcpy(code, dev->status, sizeof(int), cudaMemcpyDeviceToHost));
+    const int zero = 0;
+    KG_CUDA_TRY(cudaMemcpy(dev->status, &zero, sizeof(int), cudaMemcpyHostToDevice));
+    return KG_OK;
+}
+
+int kg_sm100_matmul(float* out, const void* lhs, const void* rhs, int in_dtype, const float* bias, long long M, long long K, long long N,
+                    void* stream) {
+    return matmul_impl(out, lhs, rhs, in_dtype, bias, M, K, N, static_cast<cudaStream_t>(stream));
+}
+
+int kg_sm100_conv2d(float* out, const void* input, const void* weight, int in_dtype, const float* bias, long long B, long long C,
+                    long long XH, long long XW, long long F, long long KH, long long KW, long long stride_h, long long stride_w,
+                    long long dilation_h, long long dilation_w, long long pad_top, long long pad_bottom, long long pad_left,
+                    long long pad_right, void* stream) {
+    kg::Conv2dShape s;
+    int rc = conv2d_shape(&s, B, C, XH, XW, F, KH, KW, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_bottom, pad_left,
+                          pad_right);
+    if (rc != KG_OK) return rc;
+    return conv2d_impl(out, input, weight, in_dtype, bias, s, static_cast<cudaStream_t>(stream));
+}
+
+int kg_sm100_flash_attention(void* out, const void* q, const void* k, const void* v, int dtype, long long B, long long H, long long S,
+                             long long D, float scale, int causal, void* stream) {
+    return flash_attention_impl(out, q, k, v, dtype, B, H, S, D, scale, causal, static_cast<cudaStream_t>(stream));
+}
+
+// Slots: (out[H,W] f32, lhs[H,K], rhs[K,W], bias[W] | absent, tile_h, tile_w, tile_k).
+int kg_sm100_matmul_entry(const KgArgSlot* slots, unsigned long long n) {
+    if (slots == nullptr || n != 7) return fail(KG_ERR_INVALID_ARGUMENT, "matmul entry expects 7 slots, got %llu", n);
+    MemArg out, lhs, rhs, bias;
+    int rc;
+    if ((rc = read_mem(slots, 0, "out", false, 2, &out)) || (rc = read_mem(slots, 1, "lhs", false, 2, &lhs)) ||
+        (rc = read_mem(slots, 2, "rhs", false, 2, &rhs)) || (rc = read_mem(slots, 3, "bias", true, 1, &bias)))
+        return rc;
+    long long tiles[3];
+    for (int t = 0; t < 3; ++t) {
+        if ((rc = read_int(slots, 4 + t, "tile", &tiles[t]))) return rc;
+        if (tiles[t] <= 0) return fail(KG_ERR_INVALID_ARGUMENT, "matmul: tile %d must be positive (%lld)", t, tiles[t]);
+    }
+    const long long H = lhs.shape[0], K = lhs.shape[1], W = rhs.shape[1];
+    if (rhs.shape[0] != K || out.shape[0] != H || out.shape[1] != W)
+        return fail(KG_ERR_INVALID_ARGUMENT, "matmul: shape mismatch out[%lld,%lld] lhs[%lld,%lld] rhs[%lld,%lld]", out.shape[0],
+                    out.shape[1], H, K, rhs.shape[0], W);
+    if (lhs.dtype != rhs.dtype) return fail(KG_ERR_INVALID_ARGUMENT, "matmul: lhs/rhs dtype mismatch (%d vs %d)", lhs.dtype, rhs.dtype);
+    if (out.dtype != KG_DTYPE_F32) return fail(KG_ERR_UNSUPPORTED, "matmul: out must be f32 (dtype code %d)", out.dtype);
+    if (bias.data && (bias.dtype != KG_DTYPE_F32 || bias.shape[0] != W))
+        return fail(KG_ERR_INVALID_ARGUMENT, "matmul: bias must be f32[%lld]", W);
+    std::lock_guard<std::mutex> call_lock(g_call_mu);
+    cudaStream_t stream = 0;
+    std::vector<MemArg*> all = {&out, &lhs, &rhs, &bias};
+    if ((rc = stage_in(all, stream))) return rc;
+    rc = matmul_impl(static_cast<float*>(out.dev), lhs.dev, rhs.dev, lhs.dtype, static_cast<const float*>(bias.dev), H, K, W, stream);
+    return finish_call(rc, &out, stream);
+}
+
+// Slots: (out, input, weight, bias | absent, sh, sw, dh, dw, pt, pb, pl, pr, tf, tc, tn, tho, two).
+int kg_sm100_conv2d_entry(const KgArgSlot* slots, unsigned long long n) {
+    if (slots == nullptr || n != 17) return fail(KG_ERR_INVALID_ARGUMENT, "conv2d entry expects 17 slots, got %llu", n);
+    MemArg out, input, weight, bias;
+    int rc;
+    if ((rc = read_mem(slots, 0, "out", false, 4, &out)) || (rc = read_mem(slots, 1, "input", false, 4, &input)) ||
+        (rc = read_mem(slots, 2, "weight", false, 4, &weight)) || (rc = read_mem(slots, 3, "bias", true, 1, &bias)))
+        return rc;
+    long long sc[13];
+    static const char* names[13] = {"stride_h", "stride_w", "dilation_h", "dilation_w", "pad_top", "pad_bottom", "pad_left",
+                                    "pad_right", "tile_f", "tile_c", "tile_n", "tile_ho", "tile_wo"};
+    for (int i = 0; i < 13; ++i) {
+        if ((rc = read_int(slots, 4 + i, names[i], &sc[i]))) return rc;
+    }
+    for (int i = 8; i < 13; ++i)
+        if (sc[i] <= 0) return fail(KG_ERR_INVALID_ARGUMENT, "conv2d: %s must be positive (%lld)", names[i], sc[i]);
+    if (input.dtype != weight.dtype) return fail(KG_ERR_INVALID_ARGUMENT, "conv2d: input/weight dtype mismatch");
+    if (out.dtype != KG_DTYPE_F32) return fail(KG_ERR_UNSUPPORTED, "conv2d: out must be f32");
+    if (weight.shape[1] != input.shape[1]) return fail(KG_ERR_INVALID_ARGUMENT, "conv2d: channel mismatch");
+    kg::Conv2dShape s;
+    if ((rc = conv2d_shape(&s, input.shape[0], input.shape[1], input.shape[2], input.shape[3], weight.shape[0], weight.shape[2],
+                           weight.shape[3], sc[0], sc[1], sc[2], sc[3], sc[4], sc[5], sc[6], sc[7])))
+        return rc;
+    if (out.shape[0] != s.B || out.shape[1] != s.F || out.shape[2] != s.HO || out.shape[3] != s.WO)
+        return fail(KG_ERR_INVALID_ARGUMENT, "conv2d: out shape mismatch (expected [%d,%d,%d,%d])", s.B, s.F, s.HO, s.WO);
+    if (bias.data && (bias.dtype != KG_DTYPE_F32 || bias.shape[0] != s.F)) return fail(KG_ERR_INVALID_ARGUMENT, "conv2d: bias must be f32[F]");
+    std::lock_guard<std::mutex> call_lock(g_call_mu);
+    cudaStream_t stream = 0;
+    std::vector<MemArg*> all = {&out, &input, &weight, &bias};
+    if ((rc = stage_in(all, stream))) return rc;
+    rc = conv2d_impl(static_cast<float*>(out.dev), input.dev, weight.dev, input.dtype, static_cast<const float*>(bias.dev), s, stream);
+    return finish_call(rc, &out, stream);
+}
+
+// Slots: (out, q, k, v, br, bc[, scale (float), causal (int)]).
+int kg_sm100_flash_attention_entry(const KgArgSlot* slots, unsigned long long n) {
+    if (slots == nullptr || (n != 6 && n != 8)) return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention entry expects 6 or 8 slots, got %llu", n);
+    MemArg out, q, k, v;
+    int rc;
+    if ((rc = read_mem(slots, 0, "out", false, 4, &out)) || (rc = read_mem(slots, 1, "q", false, 4, &q)) ||
+        (rc = read_mem(slots, 2, "k", false, 4, &k)) || (rc = read_mem(slots, 3, "v", false, 4, &v)))
+        return rc;
+    long long br, bc;
+    if ((rc = read_int(slots, 4, "br", &br)) || (rc = read_int(slots, 5, "bc", &bc))) return rc;
+    if (br <= 0 || bc <= 0) return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention: br/bc must be positive");
+    float scale = 1.0f;
+    int causal = 0;
+    if (n == 8) {
+        if (slots[6].kind == KG_SLOT_FLOAT) scale = static_cast<float>(slots[6].float_value);
+        else if (slots[6].kind == KG_SLOT_INT) scale = static_cast<float>(slots[6].int_value);
+        else return fail(KG_ERR_INVALID_ARGUMENT, "slot 6 (scale): expected float");
+        long long c;
+        if ((rc = read_int(slots, 7, "causal", &c))) return rc;
+        causal = c != 0;
+    }
+    for (int d = 0; d < 4; ++d) {
+        if (q.shape[d] != out.shape[d] || k.shape[d] != out.shape[d] || v.shape[d] != out.shape[d])
+            return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention: out/q/k/v shapes differ");
+    }
+    if (q.dtype != k.dtype || q.dtype != v.dtype || q.dtype != out.dtype)
+        return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention: out/q/k/v dtypes differ");
+    std::lock_guard<std::mutex> call_lock(g_call_mu);
+    cudaStream_t stream = 0;
+    std::vector<MemArg*> all = {&out, &q, &k, &v};
+    if ((rc = stage_in(all, stream))) return rc;
+    rc = flash_attention_impl(out.dev, q.dev, k.dev, v.dev, q.dtype, out.shape[0], out.shape[1], out.shape[2], out.shape[3], scale, causal,
+                              stream);
+    return finish_call(rc, &out, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,16 @@
+// Host-side launch interface of the tcgen05 bf16 GEMM (kg_gemm_tc.cu).
+#pragma once
+#include <cstddef>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace kg {
+size_t gemm_bf16_tc_smem_bytes();
+bool gemm_bf16_tc_supported(long long M, long long N, long long K);
+// tm_a: lhs [M,K] bf16, box 64(K) x 128(M), 128B swizzle. tm_b: rhs [K,N] bf16, box 64(N) x 64(K), 128B swizzle.
+cudaError_t gemm_bf16_tc_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_b, float* out, const float* bias, int M, int N,
+                                int K, int num_sms, int* status, cudaStream_t stream);
+int gemm_bf16_tc_tile_m();
+int gemm_bf16_tc_tile_n();
+int gemm_bf16_tc_tile_k();
+}  // namespace kg

@@ -1,0 +1,25 @@
+// Host-side launch interface of the CUDA-core kernels (kg_simt.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+namespace kg {
+
+struct Conv2dShape {
+    int B, C, XH, XW;     // input [B, C, XH, XW]
+    int F, KH, KW;        // weight [F, C, KH, KW]
+    int HO, WO;           // output [B, F, HO, WO]
+    int sh, sw, dh, dw;   // stride, dilation
+    int pt, pb, pl, pr;   // padding top, bottom, left, right
+};
+
+template <typename T>
+cudaError_t matmul_simt_launch(float* out, const T* lhs, const T* rhs, const float* bias, int M, int N, int K, cudaStream_t stream);
+
+template <typename T>
+cudaError_t conv2d_simt_launch(float* out, const T* input, const T* weight, const float* bias, const Conv2dShape& s, cudaStream_t stream);
+
+template <typename T>
+cudaError_t flash_attn_simt_launch(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
+                                   cudaStream_t stream);
+
+}  // namespace kg

@@ -1,0 +1,258 @@
+"""GPU parity: the sm_100a kernels, called through the C ABI, against the CPU oracle.
+
+* Every golden fixture (outputs of the reference's own npu_demo helpers) through the
+  reference-facing slot entry (`kg_execute_entry` shims via ExecutionEngine), with numpy
+  (host) and torch CUDA (device) memory.
+* The fp32 configurations C1-C3 at full size: rtol 1e-4 / atol 1e-5.
+* bf16 configurations: rtol 2e-2 / atol 2e-2 against fp32 maths on the bf16-rounded inputs;
+  C4 / C5 at full size through sampled rows (oracle cost) plus size-independent properties.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import golden_cases, load_golden
+from kernelcode_generate_b200 import kernels, runtime, workloads
+from kernelcode_generate_b200.execute_engine import ExecutionEngine
+
+pytestmark = pytest.mark.gpu
+
+FP32_TOL = dict(rtol=1e-4, atol=1e-5)
+BF16_TOL = dict(rtol=2e-2, atol=2e-2)
+
+WRAPPER = {
+    "matmul": "matmul_inputs_dynamic_tile_dynamic_kernel",
+    "conv2d": "conv2d_inputs_dynamic_tile_dynamic_kernel",
+    "flash_attention": "flash_attention_inputs_dynamic_tile_dynamic_kernel",
+}
+CASES = golden_cases()
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _to_torch(x, device):
+    torch = _torch()
+    if x.dtype == np.uint16:
+        return torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(device)
+    return torch.from_numpy(x).to(device)
+
+
+def _slot_args(kind, params, inputs, out):
+    if kind == "matmul":
+        return (out, inputs["lhs"], inputs["rhs"], inputs.get("bias"), *params["tiles"])
+    if kind == "conv2d":
+        return (out, inputs["input"], inputs["weight"], inputs.get("bias"), *params["stride"], *params["dilation"],
+                *params["pads"], *params["tiles"])
+    return (out, inputs["q"], inputs["k"], inputs["v"], *params["tiles"], float(params["scale"]), int(params["causal"]))
+
+
+def _out_like(kind, expected, inputs):
+    if kind == "flash_attention" and inputs["q"].dtype == np.uint16:
+        return np.zeros(expected.shape, np.uint16)
+    return np.zeros(expected.shape, np.float32)
+
+
+def _as_f32(x):
+    return workloads.bf16_bits_to_f32(x) if x.dtype == np.uint16 else x
+
+
+def _tol(inputs):
+    return BF16_TOL if any(v.dtype == np.uint16 for v in inputs.values()) else FP32_TOL
+
+
+@pytest.mark.parametrize("name,kind,params,inputs", CASES, ids=[c[0] for c in CASES])
+def test_golden_through_slot_entry_host_memory(cuda_device, name, kind, params, inputs):
+    gold = load_golden(name)["expected"]
+    out = _out_like(kind, gold, inputs)
+    kernel = ExecutionEngine(target="cuda_sm100").compile(function=WRAPPER[kind])
+    result = kernel.execute(args=_slot_args(kind, params, inputs, out))
+    assert result.ok and result.status_code == 0
+    np.testing.assert_allclose(_as_f32(out), gold, **_tol(inputs))
+
+
+@pytest.mark.parametrize("name,kind,params,inputs", CASES, ids=[c[0] for c in CASES])
+def test_golden_through_slot_entry_device_memory(cuda_device, name, kind, params, inputs):
+    torch = _torch()
+    gold = load_golden(name)["expected"]
+    dev_inputs = {k: _to_torch(v, cuda_device) for k, v in inputs.items()}
+    out = _to_torch(_out_like(kind, gold, inputs), cuda_device)
+    kernel = ExecutionEngine(target="cuda_sm100").compile(function=WRAPPER[kind])
+    kernel.execute(args=_slot_args(kind, params, dev_inputs, out))
+    got = out.float().cpu().numpy()
+    np.testing.assert_allclose(got, gold, **_tol(inputs))
+    assert runtime.device_status() == 0
+    del torch
+
+
+def test_reference_wrapper_names_run(cuda_device):
+    lhs = np.arange(6, dtype=np.float32).reshape(2, 3)
+    rhs = np.arange(12, dtype=np.float32).reshape(3, 4)
+    bias = np.arange(4, dtype=np.float32)
+    out = np.zeros((2, 4), np.float32)
+    kernels.matmul_inputs_dynamic_tile_dynamic_kernel(out, lhs, rhs, bias, 2, 2, 2)
+    np.testing.assert_allclose(out, lhs @ rhs + bias, rtol=1e-5, atol=1e-5)
+    static = ExecutionEngine(target="cuda_sm100").compile(function="matmul_inputs_static_tile_static_kernel")
+    out2 = np.zeros((2, 4), np.float32)
+    static.execute(args=(out2, lhs, rhs, None))
+    np.testing.assert_allclose(out2, lhs @ rhs, rtol=1e-5, atol=1e-5)
+
+
+# ---------------------------------------------------------------- bf16 tensor-core GEMM
+@pytest.mark.parametrize("M,K,N", [(128, 64, 256), (256, 128, 512), (200, 136, 264), (1, 8, 8), (129, 72, 40),
+                                   (384, 1024, 768), (1000, 520, 1032)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_bf16_gemm_shapes_vs_oracle(cuda_device, M, K, N, with_bias):
+    torch = _torch()
+    rng = np.random.default_rng(M * 7 + K * 3 + N)
+    a = workloads.bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
+    b = workloads.bf16_bits(rng.standard_normal((K, N), dtype=np.float32))
+    bias = rng.standard_normal(N, dtype=np.float32) if with_bias else None
+    expect = oracle.matmul(a, b, bias, tiles=(128, 256, 64))
+    out = torch.full((M, N), float("nan"), device=cuda_device)
+    kernels.matmul(out, _to_torch(a, cuda_device), _to_torch(b, cuda_device),
+                   None if bias is None else _to_torch(bias, cuda_device))
+    torch.cuda.synchronize()
+    assert runtime.device_status() == 0
+    np.testing.assert_allclose(out.cpu().numpy(), expect, **BF16_TOL)
+
+
+def test_bf16_gemm_picks_tensor_cores_and_simt_for_unaligned(cuda_device):
+    torch = _torch()
+    a = torch.randn(256, 256, device=cuda_device).bfloat16()
+    out = torch.empty(256, 256, device=cuda_device)
+    kernels.matmul(out, a, a)
+    assert runtime.last_kernel() == "gemm_bf16_tc_kernel"
+    a2 = torch.randn(64, 36, device=cuda_device).bfloat16()  # K % 8 != 0: no TMA row stride
+    b2 = torch.randn(36, 48, device=cuda_device).bfloat16()
+    out2 = torch.empty(64, 48, device=cuda_device)
+    kernels.matmul(out2, a2, b2)
+    assert runtime.last_kernel() == "matmul_simt_kernel<bf16>"
+    ref = a2.float() @ b2.float()
+    torch.testing.assert_close(out2, ref, rtol=2e-2, atol=2e-2)
+
+
+def test_c4_full_size_sampled_rows(cuda_device):
+    """C4: 8192^3 bf16 -> f32. Sampled rows vs the oracle, plus a column-sum identity on all rows."""
+    torch = _torch()
+    cfg = workloads.CONFIGS["C4"]
+    inp = workloads.make_inputs(cfg)
+    a, b = _to_torch(inp["lhs"], cuda_device), _to_torch(inp["rhs"], cuda_device)
+    M = cfg.shape["M"]
+    out = torch.empty(M, cfg.shape["N"], device=cuda_device)
+    kernels.matmul(out, a, b)
+    torch.cuda.synchronize()
+    assert runtime.device_status() == 0
+    host = out.cpu().numpy()
+    for r0 in (0, 127, 4095, 8191 - 3):
+        rows = (r0, r0 + 4)
+        expect = oracle.matmul(inp["lhs"], inp["rhs"], tiles=cfg.tiles, rows=rows)
+        np.testing.assert_allclose(host[r0:r0 + 4], expect[r0:r0 + 4], **BF16_TOL)
+    # size-independent property: ones^T (A B) == (ones^T A) B, in fp64 on the GPU
+    lhs_sum = a.double().sum(0)
+    expect_colsum = (lhs_sum @ b.double()).cpu().numpy()
+    got_colsum = out.double().sum(0).cpu().numpy()
+    np.testing.assert_allclose(got_colsum, expect_colsum, rtol=1e-3, atol=2.0)
+
+
+def test_gemm_repeatable_bitwise(cuda_device):
+    torch = _torch()
+    a = torch.randn(1024, 512, device=cuda_device).bfloat16()
+    b = torch.randn(512, 2048, device=cuda_device).bfloat16()
+    o1 = torch.empty(1024, 2048, device=cuda_device)
+    o2 = torch.empty_like(o1)
+    kernels.matmul(o1, a, b)
+    kernels.matmul(o2, a, b)
+    torch.cuda.synchronize()
+    assert torch.equal(o1, o2)
+
+
+# ---------------------------------------------------------------- flash attention
+@pytest.mark.parametrize("S,D,causal", [(128, 64, False), (257, 64, True), (300, 128, True), (1024, 128, True),
+                                        (384, 128, False), (65, 32, False)])
+def test_bf16_flash_attention_vs_oracle(cuda_device, S, D, causal):
+    torch = _torch()
+    rng = np.random.default_rng(S + D)
+    shape = (2, 3, S, D)
+    q, k, v = (workloads.bf16_bits(rng.standard_normal(shape, dtype=np.float32)) for _ in range(3))
+    scale = 1.0 / math.sqrt(D)
+    expect = oracle.flash_attention(q, k, v, tiles=(128, 128), scale=scale, causal=causal)
+    out = torch.empty(shape, dtype=torch.bfloat16, device=cuda_device)
+    kernels.flash_attention(out, _to_torch(q, cuda_device), _to_torch(k, cuda_device), _to_torch(v, cuda_device), scale, causal)
+    torch.cuda.synchronize()
+    assert runtime.device_status() == 0
+    np.testing.assert_allclose(out.float().cpu().numpy(), expect, **BF16_TOL)
+
+
+def test_c5_full_size_sampled_rows(cuda_device):
+    """C5: causal bf16 4x32x8192x128. Sampled (b,h) pairs and query rows vs the oracle (first
+    rows, a tile boundary, the last rows: the causal diagonal); every row's output is a convex
+    combination of V rows (within [min V, max V] per column)."""
+    torch = _torch()
+    cfg = workloads.CONFIGS["C5"]
+    s = cfg.shape
+    inp = workloads.make_inputs(cfg)
+    q, k, v = (_to_torch(inp[n], cuda_device) for n in ("q", "k", "v"))
+    out = torch.empty_like(q)
+    kernels.flash_attention(out, q, k, v, s["scale"], True)
+    torch.cuda.synchronize()
+    assert runtime.device_status() == 0
+    host = out.float().cpu().numpy()
+    for bh in (0, 77, 127):
+        for q0, q1 in ((0, 3), (127, 131), (8190, 8192)):
+            expect = oracle.flash_attention(inp["q"], inp["k"], inp["v"], tiles=cfg.tiles, scale=s["scale"], causal=True,
+                                            bh=(bh, bh + 1), q_rows=(q0, q1))
+            got = host.reshape(-1, s["S"], s["D"])[bh, q0:q1]
+            np.testing.assert_allclose(got, expect.reshape(-1, s["S"], s["D"])[bh, q0:q1], **BF16_TOL)
+    vf = v.float()
+    vmax = vf.amax(dim=2, keepdim=True)
+    vmin = vf.amin(dim=2, keepdim=True)
+    of = out.float()
+    assert bool(((of <= vmax + 2e-2) & (of >= vmin - 2e-2)).all())
+    # row 0 attends only to key 0: out[.., 0, :] == v[.., 0, :] (bf16 rounding)
+    torch.testing.assert_close(of[:, :, 0], vf[:, :, 0], rtol=1e-2, atol=1e-2)
+
+
+def test_flash_attention_f32_c3_typed_entry(cuda_device):
+    torch = _torch()
+    cfg = workloads.CONFIGS["C3"]
+    inp = workloads.make_inputs(cfg)
+    gold = load_golden("C3")["expected"]
+    q, k, v = (_to_torch(inp[n], cuda_device) for n in ("q", "k", "v"))
+    out = torch.empty_like(q)
+    kernels.flash_attention(out, q, k, v, cfg.shape["scale"], False)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out.cpu().numpy(), gold, **FP32_TOL)
+
+
+def test_conv2d_f32_c2_typed_entry(cuda_device):
+    torch = _torch()
+    cfg = workloads.CONFIGS["C2"]
+    inp = workloads.make_inputs(cfg)
+    gold = load_golden("C2")["expected"]
+    s = cfg.shape
+    out = torch.empty(gold.shape, device=cuda_device)
+    kernels.conv2d(out, _to_torch(inp["input"], cuda_device), _to_torch(inp["weight"], cuda_device), None, s["stride"],
+                   s["dilation"], s["pads"])
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out.cpu().numpy(), gold, **FP32_TOL)
+
+
+def test_typed_entries_report_errors_without_launching(cuda_device):
+    torch = _torch()
+    x = torch.zeros(4, 4, device=cuda_device)
+    with pytest.raises(runtime.KernelError) as e:
+        runtime.check(runtime.load().kg_sm100_matmul(x.data_ptr(), x.data_ptr(), x.data_ptr(), 9, None, 4, 4, 4, None))
+    assert e.value.code == runtime.KG_ERR_UNSUPPORTED
+    with pytest.raises(runtime.KernelError) as e:
+        runtime.check(runtime.load().kg_sm100_matmul(x.data_ptr(), x.data_ptr(), x.data_ptr(), 1, None, 0, 4, 4, None))
+    assert e.value.code == runtime.KG_ERR_INVALID_ARGUMENT
+    assert runtime.device_status() == 0
