@@ -1,0 +1,394 @@
+// bf16 flash attention forward on tcgen05 tensor cores (TMEM accumulators, TMA loads).
+//
+// Computes what the reference's online-softmax loop nest computes
+// (kernel/flash_attention/inputs_dynamic_tile_dynamic.py:117-195: per key tile S = Q K^T,
+// running max, P = exp(S - m), l = l * exp(m_old - m) + rowsum(P), O = O * exp(m_old - m) + P V,
+// finally O / l), with the extensions scale (S * scale) and causal (key > query masked).
+//
+// CTA work unit: one (b, h) and two 128-row query tiles Q0, Q1 (256 rows). Key/value tiles of 128
+// rows stream through a 2-stage TMA ring. TMEM (512 columns): S0 | S1 | O0 | O1; P_i (bf16) is
+// written back over the first half of S_i's columns and consumed from TMEM by the PV MMA.
+//   warps 0-3   softmax + epilogue for Q0 (thread = query row = TMEM lane)
+//   warps 4-7   softmax + epilogue for Q1
+//   warp 8      TMA producer (Q once; K_j, V_j per key tile)
+//   warp 9      MMA issuer (S_i = Q_i K_j^T; O_i += P_i V_j), ping-ponging the two tiles so the
+//               tensor core works on one tile while the other tile's softmax runs
+// The running max is only moved when it grows by more than 2^8 (log2 domain); O and l keep using
+// the stale max otherwise, which is exact because both are scaled by the same factor.
+#include "kg_flash_tc.h"
+#include "kg_ptx.cuh"
+
+namespace kg {
+namespace {
+
+constexpr int BM = 128;          // query rows per tile (TMEM lanes)
+constexpr int BN = 128;          // key rows per tile
+constexpr int KV_STAGES = 2;
+constexpr int NUM_THREADS = 320; // 10 warps
+constexpr float RESCALE_THRESHOLD = 8.0f;
+
+template <int D>
+struct FlashCfg {
+    static constexpr int DBLK = D / 64;                      // 64-element (128 B) column blocks
+    static constexpr uint32_t TILE_BLOCK_BYTES = 128 * 128;  // [128 rows x 64 bf16]
+    static constexpr uint32_t Q_TILE_BYTES = DBLK * TILE_BLOCK_BYTES;
+    static constexpr uint32_t KV_TILE_BYTES = DBLK * TILE_BLOCK_BYTES;
+    static constexpr uint32_t S_COL[2] = {0, 128};
+    static constexpr uint32_t O_COL[2] = {256, 256 + D};
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr uint32_t IDESC_S = idesc_f16(BM, BN, true, true, false, false);  // Q K-major, K K-major
+    static constexpr uint32_t IDESC_O = idesc_f16(BM, D, true, true, false, true);    // P (TMEM), V MN-major
+    static constexpr size_t SMEM_BYTES = 1024 + 2 * Q_TILE_BYTES + KV_STAGES * 2 * KV_TILE_BYTES + 256;
+};
+
+struct alignas(8) FlashBars {
+    uint64_t q_full;
+    uint64_t k_full[KV_STAGES];
+    uint64_t k_empty[KV_STAGES];
+    uint64_t v_full[KV_STAGES];
+    uint64_t v_empty[KV_STAGES];
+    uint64_t s_ready[2];
+    uint64_t p_ready[2];
+    uint64_t o_done[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Number of key tiles query tile i (rows q0..q0+127) must visit.
+__device__ __forceinline__ int key_tiles_for(int q0, int S, int causal) {
+    const int last_key = causal ? min(S, q0 + BM) : S;  // exclusive
+    return (last_key + BN - 1) / BN;
+}
+
+template <int D>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v, __nv_bfloat16* __restrict__ out, int S, float scale_log2,
+                        int causal, int num_pairs, int* status) {
+    using Cfg = FlashCfg<D>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sQ = smem;                                         // [2][DBLK][128 x 128 B]
+    uint8_t* sK = sQ + 2 * Cfg::Q_TILE_BYTES;                   // [KV_STAGES][DBLK][128 x 128 B]
+    uint8_t* sV = sK + KV_STAGES * Cfg::KV_TILE_BYTES;          // [KV_STAGES][DBLK][128 x 128 B]
+    FlashBars* bars = reinterpret_cast<FlashBars*>(sV + KV_STAGES * Cfg::KV_TILE_BYTES);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int bh = blockIdx.x;
+    const int pair = num_pairs - 1 - static_cast<int>(blockIdx.y);  // heaviest (latest) query rows first
+    const int m0 = pair * 2 * BM;
+    int n_tiles[2];
+    n_tiles[0] = key_tiles_for(m0, S, causal);
+    n_tiles[1] = (m0 + BM < S) ? key_tiles_for(m0 + BM, S, causal) : 0;
+    const int n_max = max(n_tiles[0], n_tiles[1]);
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bars->q_full, 1);
+        for (int s = 0; s < KV_STAGES; ++s) {
+            mbar_init(&bars->k_full[s], 1);
+            mbar_init(&bars->k_empty[s], 1);
+            mbar_init(&bars->v_full[s], 1);
+            mbar_init(&bars->v_empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bars->s_ready[i], 1);
+            mbar_init(&bars->p_ready[i], 128);
+            mbar_init(&bars->o_done[i], 1);
+        }
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 9) {
+        tmem_alloc(&bars->tmem_base, Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    volatile int* abort = &bars->abort;
+
+    if (warp == 8) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tma_prefetch_desc(&tm_q);
+            tma_prefetch_desc(&tm_k);
+            tma_prefetch_desc(&tm_v);
+            mbar_arrive_expect_tx(&bars->q_full, 2 * Cfg::Q_TILE_BYTES);
+            for (int i = 0; i < 2; ++i)
+                for (int db = 0; db < Cfg::DBLK; ++db)
+                    tma_load_3d(sQ + i * Cfg::Q_TILE_BYTES + db * Cfg::TILE_BLOCK_BYTES, &tm_q, &bars->q_full, db * 64, m0 + i * BM, bh);
+            int issued = 0;
+            for (int j = 0; j < n_max && !*abort; ++j) {
+                const int st = j % KV_STAGES;
+                const uint32_t ph = (j / KV_STAGES) & 1u;
+                if (!mbar_wait(&bars->k_empty[st], ph ^ 1u, abort, status, kDevTimeoutProducer)) break;
+                mbar_arrive_expect_tx(&bars->k_full[st], Cfg::KV_TILE_BYTES);
+                for (int db = 0; db < Cfg::DBLK; ++db)
+                    tma_load_3d(sK + st * Cfg::KV_TILE_BYTES + db * Cfg::TILE_BLOCK_BYTES, &tm_k, &bars->k_full[st], db * 64, j * BN, bh);
+                if (!mbar_wait(&bars->v_empty[st], ph ^ 1u, abort, status, kDevTimeoutProducer)) break;
+                mbar_arrive_expect_tx(&bars->v_full[st], Cfg::KV_TILE_BYTES);
+                for (int db = 0; db < Cfg::DBLK; ++db)
+                    tma_load_3d(sV + st * Cfg::KV_TILE_BYTES + db * Cfg::TILE_BLOCK_BYTES, &tm_v, &bars->v_full[st], db * 64, j * BN, bh);
+                issued = j + 1;
+            }
+            if (*abort) {
+                int keep_waiting = 0;
+                mbar_wait(&bars->q_full, 0, &keep_waiting, nullptr, 0);
+                for (int j = max(0, issued - KV_STAGES); j < issued; ++j) {
+                    const int st = j % KV_STAGES;
+                    const uint32_t ph = (j / KV_STAGES) & 1u;
+                    mbar_wait(&bars->k_full[st], ph, &keep_waiting, nullptr, 0);
+                    mbar_wait(&bars->v_full[st], ph, &keep_waiting, nullptr, 0);
+                }
+            }
+        }
+    } else if (warp == 9) {
+        // ------------------------------------------------------------ MMA issuer
+        const uint32_t q_base = smem_u32(sQ);
+        const uint32_t k_base = smem_u32(sK);
+        const uint32_t v_base = smem_u32(sV);
+        auto issue_s = [&](int i, int j) {
+            const int st = j % KV_STAGES;
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t koff = (kk / 4) * Cfg::TILE_BLOCK_BYTES + (kk % 4) * 32;
+                    const uint64_t a = smem_desc_sw128(q_base + i * Cfg::Q_TILE_BYTES + koff, 16, 1024);
+                    const uint64_t b = smem_desc_sw128(k_base + st * Cfg::KV_TILE_BYTES + koff, 16, 1024);
+                    umma_f16(tmem + Cfg::S_COL[i], a, b, Cfg::IDESC_S, kk > 0 ? 1u : 0u);
+                }
+                umma_commit(&bars->s_ready[i]);
+            }
+            __syncwarp();
+        };
+        auto issue_pv = [&](int i, int j) {
+            const int st = j % KV_STAGES;
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; ++kk) {
+                    const uint64_t b = smem_desc_sw128(v_base + st * Cfg::KV_TILE_BYTES + kk * 2048, Cfg::TILE_BLOCK_BYTES, 1024);
+                    umma_f16_ts(tmem + Cfg::O_COL[i], tmem + Cfg::S_COL[i] + kk * 8, b, Cfg::IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+                }
+            }
+            __syncwarp();
+        };
+        auto commit = [&](uint64_t* bar) {
+            if (lane == 0) umma_commit(bar);
+            __syncwarp();
+        };
+        bool ok = mbar_wait(&bars->q_full, 0, abort, status, kDevTimeoutMma);
+        if (ok && n_max > 0) {
+            ok = mbar_wait(&bars->k_full[0], 0, abort, status, kDevTimeoutMma);
+            if (ok) {
+                tc_fence_after();
+                for (int i = 0; i < 2; ++i)
+                    if (n_tiles[i] > 0) issue_s(i, 0);
+                commit(&bars->k_empty[0]);
+            }
+        }
+        for (int j = 0; ok && j < n_max; ++j) {
+            const int st = j % KV_STAGES;
+            const uint32_t ph = (j / KV_STAGES) & 1u;
+            const int nst = (j + 1) % KV_STAGES;
+            const uint32_t nph = ((j + 1) / KV_STAGES) & 1u;
+            if (!(ok = mbar_wait(&bars->v_full[st], ph, abort, status, kDevTimeoutMma))) break;
+            bool next_k_loaded = false;
+            for (int i = 0; i < 2; ++i) {
+                if (j >= n_tiles[i]) continue;
+                if (!(ok = mbar_wait(&bars->p_ready[i], j & 1u, abort, status, kDevTimeoutMma))) break;
+                tc_fence_after();
+                issue_pv(i, j);
+                if (j + 1 < n_tiles[i]) {
+                    if (!next_k_loaded) {
+                        if (!(ok = mbar_wait(&bars->k_full[nst], nph, abort, status, kDevTimeoutMma))) break;
+                        tc_fence_after();
+                        next_k_loaded = true;
+                    }
+                    issue_s(i, j + 1);
+                } else {
+                    commit(&bars->o_done[i]);
+                }
+            }
+            if (!ok) break;
+            commit(&bars->v_empty[st]);
+            if (next_k_loaded) commit(&bars->k_empty[nst]);
+        }
+        commit(&bars->drain);
+        int keep_waiting = 0;
+        mbar_wait(&bars->drain, 0, &keep_waiting, status, kDevTimeoutDrain);
+    } else {
+        // ------------------------------------------------------------ softmax + epilogue (warps 0-7)
+        const int i = warp >> 2;            // query tile of this warpgroup
+        const int quarter = warp & 3;       // TMEM lane quarter
+        const int r = quarter * 32 + lane;  // row within the tile
+        const int q0 = m0 + i * BM;
+        const int row = q0 + r;
+        const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+        const uint32_t s_addr = tmem + lane_off + Cfg::S_COL[i];
+        const uint32_t o_addr = tmem + lane_off + Cfg::O_COL[i];
+        float m_run = -INFINITY;  // running max in the log2 domain
+        float l_run = 0.0f;
+        const int n = n_tiles[i];
+        for (int j = 0; j < n; ++j) {
+            if (!mbar_wait(&bars->s_ready[i], j & 1u, abort, status, kDevTimeoutSoftmax)) break;
+            tc_fence_after();
+            float s[BN];
+#pragma unroll
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(s_addr + c * 32, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int t = 0; t < 32; ++t) s[c * 32 + t] = __uint_as_float(v[t]);
+            }
+            const int k0 = j * BN;
+            const bool need_mask = (k0 + BN > S) || (causal && k0 + BN - 1 > q0);
+            float mx = -INFINITY;
+            if (need_mask) {
+                const int lim = causal ? min(S, row + 1) : S;  // keys < lim are visible
+#pragma unroll
+                for (int t = 0; t < BN; ++t) {
+                    s[t] = (k0 + t < lim) ? s[t] * scale_log2 : -INFINITY;
+                    mx = fmaxf(mx, s[t]);
+                }
+            } else {
+#pragma unroll
+                for (int t = 0; t < BN; ++t) {
+                    s[t] *= scale_log2;
+                    mx = fmaxf(mx, s[t]);
+                }
+            }
+            float alpha = 1.0f;
+            bool rescale_o = false;
+            if (mx > m_run + RESCALE_THRESHOLD || j == 0) {
+                const float m_new = fmaxf(mx, m_run);
+                if (m_new != -INFINITY) {
+                    alpha = (m_run == -INFINITY) ? 0.0f : ex2(m_run - m_new);
+                    rescale_o = j > 0;
+                    m_run = m_new;
+                }
+            }
+            const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+            float sum = 0.0f;
+#pragma unroll
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int t = 0; t < 16; ++t) {
+                    const float p0 = ex2(s[c * 32 + 2 * t] - m_use);
+                    const float p1 = ex2(s[c * 32 + 2 * t + 1] - m_use);
+                    sum += p0 + p1;
+                    pk[t] = pack_bf16(p0, p1);
+                }
+                tmem_st_32x32b_x16(s_addr + c * 16, pk);
+            }
+            l_run = l_run * alpha + sum;
+            if (rescale_o) {
+                // s_ready(j) implies PV(j-1) has completed (tcgen05 ops complete in issue order).
+#pragma unroll 1
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(o_addr + c * 32, v);
+                    tmem_wait_ld();
+                    uint32_t w0[16], w1[16];
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) {
+                        w0[t] = __float_as_uint(__uint_as_float(v[t]) * alpha);
+                        w1[t] = __float_as_uint(__uint_as_float(v[16 + t]) * alpha);
+                    }
+                    tmem_st_32x32b_x16(o_addr + c * 32, w0);
+                    tmem_st_32x32b_x16(o_addr + c * 32 + 16, w1);
+                }
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(&bars->p_ready[i]);
+        }
+        // epilogue: O / l -> bf16 -> global
+        if (n > 0 && !*abort) {
+            if (mbar_wait(&bars->o_done[i], 0, abort, status, kDevTimeoutEpilogue)) {
+                tc_fence_after();
+                const float inv = 1.0f / l_run;
+                __nv_bfloat16* dst = out + (static_cast<size_t>(bh) * S + row) * D;
+#pragma unroll 1
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(o_addr + c * 32, v);
+                    tmem_wait_ld();
+                    if (row < S) {
+                        uint4 pk[4];
+                        uint32_t* w = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+                        for (int t = 0; t < 16; ++t)
+                            w[t] = pack_bf16(__uint_as_float(v[2 * t]) * inv, __uint_as_float(v[2 * t + 1]) * inv);
+                        uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) d4[t] = pk[t];
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 9) {
+        tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    }
+}
+
+}  // namespace
+
+bool flash_fwd_tc_supported(long long B, long long H, long long S, long long D) {
+    return (D == 64 || D == 128) && S > 0 && S < (1LL << 30) && B * H > 0 && B * H < 65536;
+}
+
+size_t flash_fwd_tc_smem_bytes(int D) { return D == 64 ? FlashCfg<64>::SMEM_BYTES : FlashCfg<128>::SMEM_BYTES; }
+
+cudaError_t flash_fwd_tc_launch(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v, __nv_bfloat16* out,
+                                int BH, int S, int D, float scale, int causal, int* status, cudaStream_t stream) {
+    const int num_pairs = (S + 2 * BM - 1) / (2 * BM);
+    const float scale_log2 = scale * 1.4426950408889634f;
+    dim3 grid(BH, num_pairs);
+    static bool attr_set[2][64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const int which = D == 64 ? 0 : 1;
+    if (dev < 0 || dev >= 64 || !attr_set[which][dev]) {
+        e = D == 64 ? cudaFuncSetAttribute(flash_fwd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)FlashCfg<64>::SMEM_BYTES)
+                    : cudaFuncSetAttribute(flash_fwd_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)FlashCfg<128>::SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) attr_set[which][dev] = true;
+    }
+    if (D == 64) {
+        flash_fwd_tc_kernel<64><<<grid, NUM_THREADS, FlashCfg<64>::SMEM_BYTES, stream>>>(tm_q, tm_k, tm_v, out, S, scale_log2, causal,
+                                                                                         num_pairs, status);
+    } else if (D == 128) {
+        flash_fwd_tc_kernel<128><<<grid, NUM_THREADS, FlashCfg<128>::SMEM_BYTES, stream>>>(tm_q, tm_k, tm_v, out, S, scale_log2,
+                                                                                           causal, num_pairs, status);
+    } else {
+        return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace kg

@@ -69,14 +69,22 @@ def _tol(inputs):
     return BF16_TOL if any(v.dtype == np.uint16 for v in inputs.values()) else FP32_TOL
 
 
+def _host(x):
+    """numpy has no bf16: host bf16 memory is a torch CPU tensor (uint16 bits reinterpreted)."""
+    if x.dtype == np.uint16:
+        return _torch().from_numpy(x.view(np.int16)).view(_torch().bfloat16)
+    return x
+
+
 @pytest.mark.parametrize("name,kind,params,inputs", CASES, ids=[c[0] for c in CASES])
 def test_golden_through_slot_entry_host_memory(cuda_device, name, kind, params, inputs):
     gold = load_golden(name)["expected"]
-    out = _out_like(kind, gold, inputs)
+    out = _host(_out_like(kind, gold, inputs))
     kernel = ExecutionEngine(target="cuda_sm100").compile(function=WRAPPER[kind])
-    result = kernel.execute(args=_slot_args(kind, params, inputs, out))
+    result = kernel.execute(args=_slot_args(kind, params, {k: _host(v) for k, v in inputs.items()}, out))
     assert result.ok and result.status_code == 0
-    np.testing.assert_allclose(_as_f32(out), gold, **_tol(inputs))
+    got = out.float().numpy() if hasattr(out, "float") else out
+    np.testing.assert_allclose(got, gold, **_tol(inputs))
 
 
 @pytest.mark.parametrize("name,kind,params,inputs", CASES, ids=[c[0] for c in CASES])
