@@ -13,6 +13,7 @@
 #include <vector>
 
 #include "../../include/kg_sm100.h"
+#include "kg_flash_tc.h"
 #include "kg_gemm_tc.h"
 #include "kg_simt.h"
 
@@ -118,6 +119,24 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long rows, long l
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// 3-D bf16 tensor map over a contiguous [BH, S, D] tensor (dims {D, S, BH}), box {64, box_rows, 1}, 128B swizzle.
+int make_tmap_3d_bf16(CUtensorMap* map, const void* base, long long BH, long long S, long long D, int box_rows) {
+    EncodeTiledFn encode = nullptr;
+    int rc = get_encode_fn(&encode);
+    if (rc != KG_OK) return rc;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(BH)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * 2, static_cast<cuuint64_t>(S) * D * 2};
+    cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+    cuuint32_t estrides[3] = {1, 1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estrides,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        return fail(KG_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d) BH=%lld S=%lld D=%lld", static_cast<int>(r), BH, S, D);
+    }
+    return KG_OK;
+}
+
 // ------------------------------------------------------------------ typed implementations
 int matmul_impl(float* out, const void* lhs, const void* rhs, int in_dtype, const float* bias, long long M, long long K, long long N,
                 cudaStream_t stream) {
@@ -197,6 +216,20 @@ int flash_attention_impl(void* out, const void* q, const void* k, const void* v,
         g_last_kernel = "flash_attn_simt_kernel<f32>";
         KG_CUDA_TRY(kg::flash_attn_simt_launch(static_cast<float*>(out), static_cast<const float*>(q), static_cast<const float*>(k),
                                                static_cast<const float*>(v), (int)B, (int)H, (int)S, (int)D, scale, causal, stream));
+        return KG_OK;
+    }
+    if (dtype == KG_DTYPE_BF16 && kg::flash_fwd_tc_supported(B, H, S, D) && aligned16(q) && aligned16(k) && aligned16(v) &&
+        aligned16(out)) {
+        DeviceInfo* dev = nullptr;
+        int rc = device_info(&dev);
+        if (rc != KG_OK) return rc;
+        CUtensorMap tq, tk, tv;
+        if ((rc = make_tmap_3d_bf16(&tq, q, B * H, S, D, 128)) || (rc = make_tmap_3d_bf16(&tk, k, B * H, S, D, 128)) ||
+            (rc = make_tmap_3d_bf16(&tv, v, B * H, S, D, 128)))
+            return rc;
+        g_last_kernel = "flash_fwd_tc_kernel";
+        KG_CUDA_TRY(kg::flash_fwd_tc_launch(tq, tk, tv, static_cast<__nv_bfloat16*>(out), (int)(B * H), (int)S, (int)D, scale, causal,
+                                            dev->status, stream));
         return KG_OK;
     }
     if (dtype == KG_DTYPE_BF16) {

@@ -33,8 +33,8 @@ struct FlashCfg {
     static constexpr uint32_t TILE_BLOCK_BYTES = 128 * 128;  // [128 rows x 64 bf16]
     static constexpr uint32_t Q_TILE_BYTES = DBLK * TILE_BLOCK_BYTES;
     static constexpr uint32_t KV_TILE_BYTES = DBLK * TILE_BLOCK_BYTES;
-    static constexpr uint32_t S_COL[2] = {0, 128};
-    static constexpr uint32_t O_COL[2] = {256, 256 + D};
+    __host__ __device__ static constexpr uint32_t s_col(int i) { return static_cast<uint32_t>(i) * 128u; }
+    __host__ __device__ static constexpr uint32_t o_col(int i) { return 256u + static_cast<uint32_t>(i) * D; }
     static constexpr uint32_t TMEM_COLS = 512;
     static constexpr uint32_t IDESC_S = idesc_f16(BM, BN, true, true, false, false);  // Q K-major, K K-major
     static constexpr uint32_t IDESC_O = idesc_f16(BM, D, true, true, false, true);    // P (TMEM), V MN-major
@@ -85,6 +85,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t* sV = sK + KV_STAGES * Cfg::KV_TILE_BYTES;          // [KV_STAGES][DBLK][128 x 128 B]
     FlashBars* bars = reinterpret_cast<FlashBars*>(sV + KV_STAGES * Cfg::KV_TILE_BYTES);
 
+    // A CTA that starts after another one reported a pipeline timeout exits at once.
+    __shared__ int skip_cta;
+    if (threadIdx.x == 0) {
+        skip_cta = status != nullptr ? *reinterpret_cast<volatile int*>(status) : 0;
+    }
+    __syncthreads();
+    if (skip_cta != 0) {
+        return;
+    }
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int bh = blockIdx.x;
@@ -170,7 +179,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint32_t koff = (kk / 4) * Cfg::TILE_BLOCK_BYTES + (kk % 4) * 32;
                     const uint64_t a = smem_desc_sw128(q_base + i * Cfg::Q_TILE_BYTES + koff, 16, 1024);
                     const uint64_t b = smem_desc_sw128(k_base + st * Cfg::KV_TILE_BYTES + koff, 16, 1024);
-                    umma_f16(tmem + Cfg::S_COL[i], a, b, Cfg::IDESC_S, kk > 0 ? 1u : 0u);
+                    umma_f16(tmem + Cfg::s_col(i), a, b, Cfg::IDESC_S, kk > 0 ? 1u : 0u);
                 }
                 umma_commit(&bars->s_ready[i]);
             }
@@ -182,7 +191,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
                     const uint64_t b = smem_desc_sw128(v_base + st * Cfg::KV_TILE_BYTES + kk * 2048, Cfg::TILE_BLOCK_BYTES, 1024);
-                    umma_f16_ts(tmem + Cfg::O_COL[i], tmem + Cfg::S_COL[i] + kk * 8, b, Cfg::IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
+                    umma_f16_ts(tmem + Cfg::o_col(i), tmem + Cfg::s_col(i) + kk * 8, b, Cfg::IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
                 }
             }
             __syncwarp();
@@ -239,8 +248,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int q0 = m0 + i * BM;
         const int row = q0 + r;
         const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-        const uint32_t s_addr = tmem + lane_off + Cfg::S_COL[i];
-        const uint32_t o_addr = tmem + lane_off + Cfg::O_COL[i];
+        const uint32_t s_addr = tmem + lane_off + Cfg::s_col(i);
+        const uint32_t o_addr = tmem + lane_off + Cfg::o_col(i);
         float m_run = -INFINITY;  // running max in the log2 domain
         float l_run = 0.0f;
         const int n = n_tiles[i];

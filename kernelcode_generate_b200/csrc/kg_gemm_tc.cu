@@ -61,6 +61,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
     Barriers* bars = reinterpret_cast<Barriers*>(sB + STAGES * B_STAGE_BYTES);
 
+    // A CTA that starts after another one reported a pipeline timeout exits at once.
+    __shared__ int skip_cta;
+    if (threadIdx.x == 0) {
+        skip_cta = status != nullptr ? *reinterpret_cast<volatile int*>(status) : 0;
+    }
+    __syncthreads();
+    if (skip_cta != 0) {
+        return;
+    }
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int num_m = (M + BM - 1) / BM;
