@@ -43,6 +43,7 @@ def parse_args(argv=None):
     ap.add_argument("--no-suite", action="store_true", help="skip the other configurations")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
     return ap.parse_args(argv)
 
 
@@ -259,30 +260,52 @@ def time_steps(wl, steps, warmup, world, flush):
     return reduce_max(total, world), total / steps, kernel
 
 
-def e2e_matmul(cfg, wl, steps, world):
-    """Metric through the slot ABI with pinned host buffers (H2D + kernel + D2H per step)."""
+def _pinned(x):
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).view(torch.bfloat16) if x.dtype == np.uint16 else torch.from_numpy(
+        np.ascontiguousarray(x))
+    return t.pin_memory()
+
+
+def e2e_run(cfg, wl, steps, world):
+    """The metric through the reference-facing slot ABI (kg_sm100_*_entry via the execute engine)
+    with pinned HOST buffers: every step copies the rank's inputs H2D, runs the kernel and copies
+    the result D2H inside the (synchronous) call."""
     import torch
 
     from kernelcode_generate_b200 import kernels
 
     s = cfg.shape
-    lhs = torch.from_numpy(wl.lhs_host.view(np.int16)).view(torch.bfloat16).pin_memory()
-    rhs = torch.from_numpy(wl.host["rhs"].view(np.int16)).view(torch.bfloat16).pin_memory()
-    out = torch.empty(wl.out.shape, dtype=torch.float32).pin_memory()
-    tiles = cfg.tiles
-    kernels.matmul_inputs_dynamic_tile_dynamic_kernel(out, lhs, rhs, None, *tiles)  # warm-up (staging arena)
+    if cfg.kernel == "matmul":
+        args = [_pinned(wl.lhs_host), _pinned(wl.host["rhs"])]
+        out = torch.empty(tuple(wl.out.shape), dtype=torch.float32).pin_memory()
+        call = lambda: kernels.matmul_inputs_dynamic_tile_dynamic_kernel(out, args[0], args[1], None, *cfg.tiles)  # noqa: E731
+    elif cfg.kernel == "flash_attention":
+        bh = s["B"] * s["H"]
+        b0, b1 = wl.rows
+        shape = (1, b1 - b0, s["S"], s["D"])
+        args = [_pinned(np.ascontiguousarray(wl.host[n].reshape(bh, s["S"], s["D"])[b0:b1]).reshape(shape)) for n in ("q", "k", "v")]
+        out = torch.empty(shape, dtype=args[0].dtype).pin_memory()
+        call = lambda: kernels.flash_attention_inputs_dynamic_tile_dynamic_kernel(out, *args, *cfg.tiles, s["scale"], s["causal"])  # noqa: E731
+    else:
+        args = [_pinned(wl.host["input"]), _pinned(wl.host["weight"])]
+        out = torch.empty(tuple(wl.out.shape), dtype=torch.float32).pin_memory()
+        call = lambda: kernels.conv2d_inputs_dynamic_tile_dynamic_kernel(  # noqa: E731
+            out, args[0], args[1], None, *s["stride"], *s["dilation"], *s["pads"], *cfg.tiles)
+    call()  # warm-up (sizes the staging arena)
     barrier(world)
     t0 = time.perf_counter()
     for _ in range(steps):
-        kernels.matmul_inputs_dynamic_tile_dynamic_kernel(out, lhs, rhs, None, *tiles)
+        call()
     barrier(world)
     elapsed = reduce_max(time.perf_counter() - t0, world)
-    total_flops = 2 * s["M"] * s["N"] * s["K"]
-    h2d = lhs.numel() * 2 + rhs.numel() * 2
-    d2h = out.numel() * 4
+    total_flops = reduce_sum(float(wl.flops), world)
+    h2d = sum(a.numel() * a.element_size() for a in args)
+    d2h = out.numel() * out.element_size()
     return {"value": round(total_flops * steps / elapsed / 1e12, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "ms_per_step": round(elapsed / steps * 1e3, 3),
-            "path": "kg_sm100_matmul_entry (slot ABI), pinned host buffers"}
+            "path": f"{cfg.kernel} slot entry (kg_execute_entry ABI) on pinned host buffers, wall clock, max over ranks"}
 
 
 # ---------------------------------------------------------------- CPU reference / baseline
@@ -398,7 +421,9 @@ def main(argv=None):
     achieved = wl.flops / (launch_ms * 1e-3) / 1e12  # this rank's kernel, algorithmic FLOPs per launch
     tensor_peak = peaks["bf16_tflops"]
     traffic = load_traffic(kernel, cfg.name)
-    e2e = e2e_matmul(cfg, wl, args.e2e_steps, world) if cfg.kernel == "matmul" and cfg.dtype == "bf16" else None
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_run(cfg, wl, args.e2e_steps, world)
 
     suite = {}
     if not args.no_suite:
