@@ -36,7 +36,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="C4", choices=["C1", "C2", "C3", "C4", "C5"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -83,7 +83,7 @@ class ClockSampler:
             self.path = out_dir / f"clocks_rank{os.environ.get('RANK', '0')}.csv"
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms",
-                                          "100", "-i", str(self.device_index)], stdout=self.fh, stderr=subprocess.DEVNULL)
+                                          "20", "-i", str(self.device_index)], stdout=self.fh, stderr=subprocess.DEVNULL)
             time.sleep(0.25)
         except (OSError, FileNotFoundError):
             self.proc = None

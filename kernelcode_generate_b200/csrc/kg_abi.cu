@@ -218,8 +218,8 @@ int flash_attention_impl(void* out, const void* q, const void* k, const void* v,
                                                static_cast<const float*>(v), (int)B, (int)H, (int)S, (int)D, scale, causal, stream));
         return KG_OK;
     }
-    if (dtype == KG_DTYPE_BF16 && kg::flash_fwd_tc_supported(B, H, S, D) && aligned16(q) && aligned16(k) && aligned16(v) &&
-        aligned16(out)) {
+    if (dtype == KG_DTYPE_BF16 && scale > 0.0f && kg::flash_fwd_tc_supported(B, H, S, D) && aligned16(q) && aligned16(k) &&
+        aligned16(v) && aligned16(out)) {
         DeviceInfo* dev = nullptr;
         int rc = device_info(&dev);
         if (rc != KG_OK) return rc;

@@ -61,6 +61,59 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+#ifndef KG_FA_POLY_PAIRS
+#define KG_FA_POLY_PAIRS 0
+#endif
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float m;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+    return m;
+}
+
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+
+__device__ __forceinline__ void unpack_f32x2(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// 2^x for two values on the FMA/ALU pipes (no MUFU, no conversion instructions):
+// x = n + f with n = round(x) found by adding 1.5 * 2^23 (n lands in the low mantissa bits),
+// f = x - n in [-0.5, 0.5]; 2^f by a cubic fitted here (weighted least squares iterated
+// towards minimax relative error on [-0.5, 0.5], p(0) = 1); n is added into the exponent field.
+// Checked in float32 against exp2 over [-126, 8]: max relative error 1.0e-4, well below the
+// 3.9e-3 of the bf16 rounding P goes through. Inputs below -126 are clamped (results ~1e-38).
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+    const uint64_t x = pack_f32x2(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
+    const uint64_t t = add_f32x2(x, pack_f32x2(12582912.0f, 12582912.0f));
+    const uint64_t n = add_f32x2(t, pack_f32x2(-12582912.0f, -12582912.0f));
+    const uint64_t f = fma_f32x2(n, pack_f32x2(-1.0f, -1.0f), x);
+    uint64_t p = fma_f32x2(pack_f32x2(0.05500871f, 0.05500871f), f, pack_f32x2(0.24221054f, 0.24221054f));
+    p = fma_f32x2(p, f, pack_f32x2(0.6932829f, 0.6932829f));
+    p = fma_f32x2(p, f, pack_f32x2(1.0f, 1.0f));
+    float p0, p1, t0, t1;
+    unpack_f32x2(p, p0, p1);
+    unpack_f32x2(t, t0, t1);
+    y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+    y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
@@ -96,13 +149,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int bh = blockIdx.x;
-    const int pair = num_pairs - 1 - static_cast<int>(blockIdx.y);  // heaviest (latest) query rows first
+    // x walks the query-tile pairs of one (b, h) so co-resident CTAs share that head's K/V in L2;
+    // within a head the heaviest (latest, for causal) pairs start first.
+    const int bh = blockIdx.y;
+    const int pair = num_pairs - 1 - static_cast<int>(blockIdx.x);
     const int m0 = pair * 2 * BM;
-    int n_tiles[2];
-    n_tiles[0] = key_tiles_for(m0, S, causal);
-    n_tiles[1] = (m0 + BM < S) ? key_tiles_for(m0 + BM, S, causal) : 0;
-    const int n_max = max(n_tiles[0], n_tiles[1]);
+    const int n_tiles0 = key_tiles_for(m0, S, causal);
+    const int n_tiles1 = (m0 + BM < S) ? key_tiles_for(m0 + BM, S, causal) : 0;
+    const int n_max = max(n_tiles0, n_tiles1);
+    auto n_tiles = [&](int i) { return i == 0 ? n_tiles0 : n_tiles1; };
 
     if (threadIdx.x == 0) {
         mbar_init(&bars->q_full, 1);
@@ -205,8 +260,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             ok = mbar_wait(&bars->k_full[0], 0, abort, status, kDevTimeoutMma);
             if (ok) {
                 tc_fence_after();
+#pragma unroll
                 for (int i = 0; i < 2; ++i)
-                    if (n_tiles[i] > 0) issue_s(i, 0);
+                    if (n_tiles(i) > 0) issue_s(i, 0);
                 commit(&bars->k_empty[0]);
             }
         }
@@ -217,12 +273,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint32_t nph = ((j + 1) / KV_STAGES) & 1u;
             if (!(ok = mbar_wait(&bars->v_full[st], ph, abort, status, kDevTimeoutMma))) break;
             bool next_k_loaded = false;
+#pragma unroll
             for (int i = 0; i < 2; ++i) {
-                if (j >= n_tiles[i]) continue;
+                if (j >= n_tiles(i)) continue;
                 if (!(ok = mbar_wait(&bars->p_ready[i], j & 1u, abort, status, kDevTimeoutMma))) break;
                 tc_fence_after();
                 issue_pv(i, j);
-                if (j + 1 < n_tiles[i]) {
+                if (j + 1 < n_tiles(i)) {
                     if (!next_k_loaded) {
                         if (!(ok = mbar_wait(&bars->k_full[nst], nph, abort, status, kDevTimeoutMma))) break;
                         tc_fence_after();
@@ -252,36 +309,33 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t o_addr = tmem + lane_off + Cfg::o_col(i);
         float m_run = -INFINITY;  // running max in the log2 domain
         float l_run = 0.0f;
-        const int n = n_tiles[i];
+        const int n = n_tiles(i);
         for (int j = 0; j < n; ++j) {
             if (!mbar_wait(&bars->s_ready[i], j & 1u, abort, status, kDevTimeoutSoftmax)) break;
             tc_fence_after();
-            float s[BN];
+            // Scores of this row: 128 f32 in registers.
+            // All four TMEM loads are in flight before the single wait.
+            uint32_t sv[BN / 32][32];
 #pragma unroll
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t v[32];
-                tmem_ld_32x32b_x32(s_addr + c * 32, v);
-                tmem_wait_ld();
+            for (int c = 0; c < BN / 32; ++c) tmem_ld_32x32b_x32(s_addr + c * 32, sv[c]);
+            tmem_wait_ld();
+            float sc[BN];
 #pragma unroll
-                for (int t = 0; t < 32; ++t) s[c * 32 + t] = __uint_as_float(v[t]);
-            }
+            for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+                for (int t = 0; t < 32; ++t) sc[c * 32 + t] = __uint_as_float(sv[c][t]);
             const int k0 = j * BN;
-            const bool need_mask = (k0 + BN > S) || (causal && k0 + BN - 1 > q0);
-            float mx = -INFINITY;
-            if (need_mask) {
-                const int lim = causal ? min(S, row + 1) : S;  // keys < lim are visible
+            if ((k0 + BN > S) || (causal && k0 + BN - 1 > q0)) {
+                const int lim = (causal ? min(S, row + 1) : S) - k0;  // columns < lim are visible
 #pragma unroll
-                for (int t = 0; t < BN; ++t) {
-                    s[t] = (k0 + t < lim) ? s[t] * scale_log2 : -INFINITY;
-                    mx = fmaxf(mx, s[t]);
-                }
-            } else {
-#pragma unroll
-                for (int t = 0; t < BN; ++t) {
-                    s[t] *= scale_log2;
-                    mx = fmaxf(mx, s[t]);
-                }
+                for (int t = 0; t < BN; ++t) sc[t] = t < lim ? sc[t] : -INFINITY;
             }
+            // Row maximum of the raw scores (scale_log2 > 0, so it commutes with the scaling).
+            float mx = max3(sc[0], sc[1], sc[2]);
+#pragma unroll
+            for (int t = 3; t + 1 < BN; t += 2) mx = max3(mx, sc[t], sc[t + 1]);
+            mx = fmaxf(mx, sc[BN - 1]);
+            mx *= scale_log2;
             float alpha = 1.0f;
             bool rescale_o = false;
             if (mx > m_run + RESCALE_THRESHOLD || j == 0) {
@@ -293,19 +347,35 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-            float sum = 0.0f;
+            // P = 2^(s * scale_log2 - m) as bf16, written over the first half of S's columns (chunk c
+            // writes columns 16c..16c+15, already read above). KG_FA_POLY_PAIRS of every 16 pairs use
+            // the FMA-pipe polynomial instead of the MUFU ex2 unit, which is the softmax bottleneck.
+            const uint64_t scale2 = pack_f32x2(scale_log2, scale_log2);
+            const uint64_t negm2 = pack_f32x2(-m_use, -m_use);
+            uint64_t sum2 = pack_f32x2(0.0f, 0.0f);
 #pragma unroll
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t pk[16];
 #pragma unroll
                 for (int t = 0; t < 16; ++t) {
-                    const float p0 = ex2(s[c * 32 + 2 * t] - m_use);
-                    const float p1 = ex2(s[c * 32 + 2 * t + 1] - m_use);
-                    sum += p0 + p1;
+                    const uint64_t x2 = fma_f32x2(pack_f32x2(sc[c * 32 + 2 * t], sc[c * 32 + 2 * t + 1]), scale2, negm2);
+                    float x0, x1;
+                    unpack_f32x2(x2, x0, x1);
+                    float p0, p1;
+                    if (t < KG_FA_POLY_PAIRS) {
+                        exp2_poly2(x0, x1, p0, p1);
+                    } else {
+                        p0 = ex2(x0);
+                        p1 = ex2(x1);
+                    }
+                    sum2 = add_f32x2(sum2, pack_f32x2(p0, p1));
                     pk[t] = pack_bf16(p0, p1);
                 }
                 tmem_st_32x32b_x16(s_addr + c * 16, pk);
             }
+            float sum_lo, sum_hi;
+            unpack_f32x2(sum2, sum_lo, sum_hi);
+            const float sum = sum_lo + sum_hi;
             l_run = l_run * alpha + sum;
             if (rescale_o) {
                 // s_ready(j) implies PV(j-1) has completed (tcgen05 ops complete in issue order).
@@ -374,7 +444,7 @@ cudaError_t flash_fwd_tc_launch(const CUtensorMap& tm_q, const CUtensorMap& tm_k
                                 int BH, int S, int D, float scale, int causal, int* status, cudaStream_t stream) {
     const int num_pairs = (S + 2 * BM - 1) / (2 * BM);
     const float scale_log2 = scale * 1.4426950408889634f;
-    dim3 grid(BH, num_pairs);
+    dim3 grid(num_pairs, BH);
     static bool attr_set[2][64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
