@@ -143,29 +143,30 @@ def barrier(world):
 
     if world > 1:
         dist.barrier()
-    torch.cuda.synchronize()
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+
+
+def _reduce(value: float, world: int, op_name: str) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return value
+    device = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=getattr(dist.ReduceOp, op_name))
+    return float(t.item())
 
 
 def reduce_max(value: float, world: int) -> float:
-    import torch
-    import torch.distributed as dist
-
-    if world == 1:
-        return value
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    """Max over ranks (job time = the slowest rank)."""
+    return _reduce(value, world, "MAX")
 
 
 def reduce_sum(value: float, world: int) -> float:
-    import torch
-    import torch.distributed as dist
-
-    if world == 1:
-        return value
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    """Sum over ranks (total work of the job)."""
+    return _reduce(value, world, "SUM")
 
 
 # ---------------------------------------------------------------- workloads on the device

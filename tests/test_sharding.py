@@ -1,0 +1,85 @@
+"""Multi-process host logic of the sharded bench path, on CPU with the gloo backend
+(world size 2): the shards tile the work exactly, per-rank oracle results assemble into the
+single-process result (the partition needs no exchange), and the timing reductions take the
+max / sum over ranks."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+import bench
+import oracle
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("total,world", [(8192, 1), (8192, 2), (8192, 8), (128, 8), (7, 3), (5, 8)])
+def test_shard_ranges_tile_the_work(total, world):
+    ranges = [bench.shard_range(total, r, world) for r in range(world)]
+    assert ranges[0][0] == 0 and ranges[-1][1] == total
+    for (a0, a1), (b0, b1) in zip(ranges, ranges[1:]):
+        assert a1 == b0 and a0 <= a1
+    sizes = [b - a for a, b in ranges]
+    assert max(sizes) - min(sizes) <= 1
+
+
+def _worker(rank, world, port, results):
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(3)
+        a = rng.standard_normal((37, 24), dtype=np.float32)
+        b = rng.standard_normal((24, 19), dtype=np.float32)
+        r0, r1 = bench.shard_range(a.shape[0], rank, world)
+        part = oracle.matmul(np.ascontiguousarray(a[r0:r1]), b, tiles=(8, 8, 8))
+        q, k, v = (rng.standard_normal((2, 3, 40, 16), dtype=np.float32) for _ in range(3))
+        b0, b1 = bench.shard_range(6, rank, world)
+        shard = lambda x: np.ascontiguousarray(x.reshape(6, 40, 16)[b0:b1]).reshape(1, b1 - b0, 40, 16)  # noqa: E731
+        fa = oracle.flash_attention(shard(q), shard(k), shard(v), tiles=(16, 16), scale=0.25, causal=True)
+        # assemble on every rank with a gather of variable-size pieces (padded)
+        pieces = [None] * world
+        dist.all_gather_object(pieces, (r0, part, b0, fa))
+        slowest = bench.reduce_max(float(rank + 1), world)
+        total = bench.reduce_sum(float(r1 - r0), world)
+        if rank == 0:
+            results.put((pieces, slowest, total))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_and_head_sharding_need_no_exchange():
+    world = 2
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    pieces, slowest, total = results.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal((37, 24), dtype=np.float32)
+    b = rng.standard_normal((24, 19), dtype=np.float32)
+    full = oracle.matmul(a, b, tiles=(8, 8, 8))
+    assembled = np.concatenate([p[1] for p in sorted(pieces, key=lambda x: x[0])], axis=0)
+    np.testing.assert_array_equal(assembled, full)
+    q, k, v = (rng.standard_normal((2, 3, 40, 16), dtype=np.float32) for _ in range(3))
+    fa_full = oracle.flash_attention(q, k, v, tiles=(16, 16), scale=0.25, causal=True).reshape(6, 40, 16)
+    fa_assembled = np.concatenate([p[3].reshape(-1, 40, 16) for p in sorted(pieces, key=lambda x: x[2])], axis=0)
+    np.testing.assert_array_equal(fa_assembled, fa_full)
+    assert slowest == 2.0 and total == 37.0
