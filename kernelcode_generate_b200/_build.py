@@ -95,6 +95,20 @@ def build(verbose: bool = False) -> Path:
     return lib
 
 
+API_CHECKS_SRC = REPO_DIR / "tests" / "cuda_api" / "api_checks.cu"
+API_CHECKS_LIB = REPO_DIR / "tests" / "_build" / "libkg_api_checks.so"
+
+
+def build_api_checks() -> Path:
+    """Compile the device checks of the include/cuda_sm100 operator surface (tests only)."""
+    deps = [API_CHECKS_SRC] + sorted((INCLUDE_DIR / "cuda_sm100").glob("*.h"))
+    if _stale(API_CHECKS_LIB, deps):
+        API_CHECKS_LIB.parent.mkdir(exist_ok=True)
+        _run([nvcc(), *ARCH_FLAGS, "-O2", "-std=c++17", "-Xcompiler", "-fPIC", "-shared", "-cudart", "static", "-I", str(INCLUDE_DIR),
+              str(API_CHECKS_SRC), "-o", str(API_CHECKS_LIB)])
+    return API_CHECKS_LIB
+
+
 def clean() -> None:
     shutil.rmtree(OBJ_DIR, ignore_errors=True)
     for p in LIB_DIR.glob("*.so"):
