@@ -17,6 +17,21 @@ namespace cuda_sm100 {
 
 namespace detail {
 
+// acc + a * b with the product and the sum rounded separately (no fused multiply-add), as the
+// npu_demo helpers compute it on the host; keeps results bit-identical to theirs.
+template <typename T>
+__device__ inline T mul_add_rn(T acc, T a, T b) {
+    return static_cast<T>(acc + a * b);
+}
+template <>
+__device__ inline float mul_add_rn<float>(float acc, float a, float b) {
+    return __fadd_rn(acc, __fmul_rn(a, b));
+}
+template <>
+__device__ inline double mul_add_rn<double>(double acc, double a, double b) {
+    return __dadd_rn(acc, __dmul_rn(a, b));
+}
+
 template <typename A, typename B>
 __device__ inline bool same_shape(const A& a, const B& b) {
     if (a.rank() != b.rank()) return false;
@@ -163,7 +178,8 @@ __device__ inline Status reduce_max(Context& ctx, Memory<Space, OutType>& out, c
     return detail::reduce2d(out, input, axis, [](OutType a, OutType b) { return b > a ? b : a; }, true);
 }
 
-// out[m,n] (+)= sum_k lhs[m,k] * rhs[k,n], accumulated in OutType in k order.
+// out[m,n] (+)= sum_k lhs[m,k] * rhs[k,n], accumulated in OutType in k order, each product and
+// sum rounded separately.
 template <MemorySpace LhsSpace, MemorySpace RhsSpace, MemorySpace OutSpace, typename LhsType, typename RhsType, typename OutType,
           typename Context>
 __device__ inline Status matmul(Context& ctx, Memory<OutSpace, OutType>& out, const Memory<LhsSpace, LhsType>& lhs,
@@ -180,7 +196,7 @@ __device__ inline Status matmul(Context& ctx, Memory<OutSpace, OutType>& out, co
         for (long long ki = 0; ki < k; ++ki) {
             lx[1] = ki;
             rx[0] = ki;
-            a = static_cast<OutType>(a + static_cast<OutType>(lhs.at(lx)) * static_cast<OutType>(rhs.at(rx)));
+            a = detail::mul_add_rn<OutType>(a, static_cast<OutType>(lhs.at(lx)), static_cast<OutType>(rhs.at(rx)));
         }
         out.at(ox) = a;
     }

@@ -66,8 +66,8 @@ def test_matmul_loop_nest_on_helpers_bit_exact(checks, cuda_device, name, kind, 
     W = inputs["rhs"].shape[1]
     out = torch.full((H, W), float("nan"), device=cuda_device)
     status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
-    rc = checks.kg_api_matmul(out.data_ptr(), _ptr(_dev(inputs["lhs"], cuda_device)), _ptr(_dev(inputs["rhs"], cuda_device)),
-                              _ptr(_dev(inputs.get("bias"), cuda_device)), H, K, W, *params["tiles"], status.data_ptr())
+    lhs, rhs, bias = (_dev(inputs.get(n), cuda_device) for n in ("lhs", "rhs", "bias"))  # kept alive across the call
+    rc = checks.kg_api_matmul(out.data_ptr(), _ptr(lhs), _ptr(rhs), _ptr(bias), H, K, W, *params["tiles"], status.data_ptr())
     assert rc == 0 and int(status.item()) == 0
     np.testing.assert_array_equal(out.cpu().numpy(), gold)
 
@@ -83,8 +83,8 @@ def test_conv2d_loop_nest_on_helpers_bit_exact(checks, cuda_device, name, kind, 
     p = np.array([B, C, XH, XW, F, KH, KW, *params["stride"], *params["dilation"], *params["pads"], *params["tiles"]], dtype=np.int64)
     out = torch.full(gold.shape, float("nan"), device=cuda_device)
     status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
-    rc = checks.kg_api_conv2d(out.data_ptr(), _ptr(_dev(x, cuda_device)), _ptr(_dev(w, cuda_device)),
-                              _ptr(_dev(inputs.get("bias"), cuda_device)), p.ctypes.data, status.data_ptr())
+    xd, wd, bd = _dev(x, cuda_device), _dev(w, cuda_device), _dev(inputs.get("bias"), cuda_device)
+    rc = checks.kg_api_conv2d(out.data_ptr(), _ptr(xd), _ptr(wd), _ptr(bd), p.ctypes.data, status.data_ptr())
     assert rc == 0 and int(status.item()) == 0
     np.testing.assert_array_equal(out.cpu().numpy(), gold)
 
@@ -106,7 +106,8 @@ def test_flash_loop_nest_on_helpers(checks, cuda_device, cfg_name, tiles):
     B, H, S, D = q.shape
     out = torch.full(q.shape, float("nan"), device=cuda_device)
     status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
-    rc = checks.kg_api_flash(out.data_ptr(), *(_ptr(_dev(t, cuda_device)) for t in (q, k, v)), B, H, S, D, *tiles, status.data_ptr())
+    qkv = [_dev(t, cuda_device) for t in (q, k, v)]
+    rc = checks.kg_api_flash(out.data_ptr(), *(_ptr(t) for t in qkv), B, H, S, D, *tiles, status.data_ptr())
     assert rc == 0 and int(status.item()) == 0
     got = out.cpu().numpy()
     # Same arithmetic as the port; exp/div go through double on both sides (CUDA's and glibc's exp
