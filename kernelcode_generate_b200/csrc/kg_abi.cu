@@ -153,6 +153,11 @@ int matmul_impl(float* out, const void* lhs, const void* rhs, int in_dtype, cons
             if (rc != KG_OK) return rc;
             rc = make_tmap_2d_bf16(&tb, rhs, K, N, 64, 64);
             if (rc != KG_OK) return rc;
+            if (M >= 256 && N >= 256 && dev->num_sms >= 2) {
+                g_last_kernel = "gemm_bf16_tc_pair_kernel";
+                KG_CUDA_TRY(kg::gemm_bf16_tc_pair_launch(ta, tb, out, bias, (int)M, (int)N, (int)K, dev->num_sms, dev->status, stream));
+                return KG_OK;
+            }
             g_last_kernel = "gemm_bf16_tc_kernel";
             KG_CUDA_TRY(kg::gemm_bf16_tc_launch(ta, tb, out, bias, (int)M, (int)N, (int)K, dev->num_sms, dev->status, stream));
             return KG_OK;

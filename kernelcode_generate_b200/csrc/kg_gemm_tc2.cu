@@ -1,0 +1,270 @@
+// bf16 x bf16 -> f32 GEMM on CTA pairs (tcgen05.mma.cta_group::2): 256 x 256 output tiles.
+//
+// Same contract as kg_gemm_tc.cu (the reference matmul loop nest,
+// kernel/matmul/inputs_dynamic_tile_dynamic.py:84-113): out[M,N] = lhs[M,K] . rhs[K,N] (+ bias[N]).
+//
+// Two CTAs of a cluster share one 256 x 256 tile: each loads its own 128 rows of A and its own
+// 128 columns of B (so each CTA streams half the B bytes of the single-CTA 128 x 256 kernel), the
+// even CTA issues one M=256 UMMA that reads both CTAs' shared memory and writes both CTAs' TMEM
+// (each holds its 128 rows x 256 f32 columns). Per CTA:
+//   warp 0      TMA producer, 6-stage ring of 32 KB (A 128x64, B 64x128); completion bytes of both
+//               CTAs are counted on the even CTA's barrier; no multicast loads.
+//   warp 1      (even CTA) MMA issuer: 4 x tcgen05.mma.cta_group::2 256x256x16 per stage, commits
+//               multicast to both CTAs' stage-release and accumulator-ready barriers.
+//   warps 2..5  epilogue of this CTA's 128 rows; releases the accumulator on the even CTA.
+#include "kg_gemm_tc.h"
+#include "kg_ptx.cuh"
+
+namespace kg {
+namespace {
+
+constexpr int PBM = 256;  // pair tile rows (128 per CTA)
+constexpr int PBN = 256;  // pair tile columns (128 of B per CTA)
+constexpr int BK = 64;
+constexpr int STAGES = 6;
+constexpr int GROUP_M = 8;
+constexpr int NUM_THREADS = 192;
+constexpr uint32_t A_STAGE_BYTES = 128 * BK * 2;  // 16 KiB
+constexpr uint32_t B_STAGE_BYTES = BK * 128 * 2;  // 16 KiB (this CTA's half of B)
+constexpr uint32_t B_BOX_BYTES = BK * 64 * 2;     // one 64(N) x 64(K) box
+constexpr uint32_t TMEM_COLS = 2 * PBN;
+constexpr uint32_t IDESC = idesc_f16(PBM, PBN, true, true, false, true);
+constexpr uint16_t PAIR_MASK = 0x3;
+
+struct alignas(8) PairBarriers {
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t tfull[2];
+    uint64_t tempty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + sizeof(PairBarriers);
+
+__device__ __forceinline__ void pair_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+    const int per_group = GROUP_M * num_n;
+    const int group = tile / per_group;
+    const int first_m = group * GROUP_M;
+    const int gsize = min(num_m - first_m, GROUP_M);
+    const int in_group = tile - group * per_group;
+    mb = first_m + in_group % gsize;
+    nb = in_group / gsize;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, float* __restrict__ out,
+                             const float* __restrict__ bias, int M, int N, int K, int vec_ok, int* status) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+    PairBarriers* bars = reinterpret_cast<PairBarriers*>(sB + STAGES * B_STAGE_BYTES);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1;
+    const int num_pairs = gridDim.x >> 1;
+    const int num_m = (M + PBM - 1) / PBM;
+    const int num_n = (N + PBN - 1) / PBN;
+    const int num_tiles = num_m * num_n;
+    const int num_kb = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&bars->tfull[a], 1);
+            mbar_init(&bars->tempty[a], 8);  // lane 0 of the 4 epilogue warps of both CTAs
+        }
+        mbar_init(&bars->drain, 1);
+        // A kernel that starts after another reported a pipeline timeout does no work.
+        bars->abort = (status != nullptr && *reinterpret_cast<volatile int*>(status) != 0) ? 1 : 0;
+        fence_barrier_init();
+        tma_prefetch_desc(&tm_a);
+        tma_prefetch_desc(&tm_b);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(&bars->tmem_base, TMEM_COLS);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or completion
+    tc_fence_after();
+    const uint32_t tmem_base = bars->tmem_base;
+    volatile int* abort = &bars->abort;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer (both CTAs)
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued = 0;
+            for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs) {
+                int mb, nb;
+                pair_tile_coords(tile, num_m, num_n, mb, nb);
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait_cluster(&bars->empty[stage], phase ^ 1u, abort, status, kDevTimeoutProducer)) break;
+                    if (leader) mbar_arrive_expect_tx(&bars->full[stage], 2 * (A_STAGE_BYTES + B_STAGE_BYTES));
+                    const uint32_t leader_full = mapa_shared(smem_u32(&bars->full[stage]), 0);
+                    tma_load_2d_pair(sA + stage * A_STAGE_BYTES, &tm_a, leader_full, kb * BK, mb * PBM + static_cast<int>(rank) * 128);
+                    uint8_t* b_dst = sB + stage * B_STAGE_BYTES;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                        tma_load_2d_pair(b_dst + j * B_BOX_BYTES, &tm_b, leader_full, nb * PBN + static_cast<int>(rank) * 128 + j * 64, kb * BK);
+                    ++issued;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (*abort && leader) {
+                // The even CTA's full barriers count both CTAs' bytes: wait (bounded) for the copies
+                // still in flight before the pair's shared memory goes away.
+                const uint32_t pending = issued < STAGES ? issued : STAGES;
+                int keep_waiting = 0;
+                for (uint32_t i = 0; i < pending; ++i) {
+                    stage = stage == 0 ? STAGES - 1 : stage - 1;
+                    if (stage == STAGES - 1) phase ^= 1u;
+                    mbar_wait_cluster(&bars->full[stage], phase, &keep_waiting, nullptr, 0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer (even CTA)
+        if (leader) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t acc = 0, acc_phase = 0;
+            for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs) {
+                if (!mbar_wait_cluster(&bars->tempty[acc], acc_phase ^ 1u, abort, status, kDevTimeoutMma)) break;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + acc * PBN;
+                bool ok = true;
+                for (int kb = 0; kb < num_kb; ++kb) {
+                    if (!mbar_wait_cluster(&bars->full[stage], phase, abort, status, kDevTimeoutMma)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
+                        const uint32_t b_base = smem_u32(sB + stage * B_STAGE_BYTES);
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk) {
+                            const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
+                            const uint64_t b_desc = smem_desc_sw128(b_base + kk * 2048, B_BOX_BYTES, 1024);
+                            umma_f16_pair(d_tmem, a_desc, b_desc, IDESC, (kb | kk) != 0 ? 1u : 0u);
+                        }
+                        umma_commit_pair_multicast(&bars->empty[stage], PAIR_MASK);
+                    }
+                    __syncwarp();
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                if (lane == 0) umma_commit_pair_multicast(&bars->tfull[acc], PAIR_MASK);
+                __syncwarp();
+                acc ^= 1u;
+                if (acc == 0) acc_phase ^= 1u;
+            }
+            if (lane == 0) umma_commit_pair(&bars->drain);
+            __syncwarp();
+            int keep_waiting = 0;
+            mbar_wait_cluster(&bars->drain, 0, &keep_waiting, status, kDevTimeoutDrain);
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+        const int quarter = warp & 3;
+        const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&bars->tempty[0]), 0), mapa_shared(smem_u32(&bars->tempty[1]), 0)};
+        uint32_t acc = 0, acc_phase = 0;
+        for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs) {
+            int mb, nb;
+            pair_tile_coords(tile, num_m, num_n, mb, nb);
+            if (!mbar_wait_cluster(&bars->tfull[acc], acc_phase, abort, status, kDevTimeoutEpilogue)) break;
+            tc_fence_after();
+            const int row = mb * PBM + static_cast<int>(rank) * 128 + quarter * 32 + lane;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * PBN;
+#pragma unroll 1
+            for (int c = 0; c < PBN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(t_row + c * 32, r);
+                tmem_wait_ld();
+                if (c == PBN / 32 - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+                }
+                const int col0 = nb * PBN + c * 32;
+                if (row < M) {
+                    float* dst = out + static_cast<size_t>(row) * N + col0;
+                    if (vec_ok && col0 + 32 <= N) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            float4 v = make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]), __uint_as_float(r[i + 2]),
+                                                   __uint_as_float(r[i + 3]));
+                            if (bias != nullptr) {
+                                const float4 bv = *reinterpret_cast<const float4*>(bias + col0 + i);
+                                v.x += bv.x;
+                                v.y += bv.y;
+                                v.z += bv.z;
+                                v.w += bv.w;
+                            }
+                            *reinterpret_cast<float4*>(dst + i) = v;
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            if (col0 + i < N) dst[i] = __uint_as_float(r[i]) + (bias != nullptr ? bias[col0 + i] : 0.0f);
+                        }
+                    }
+                }
+            }
+            acc ^= 1u;
+            if (acc == 0) acc_phase ^= 1u;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // no CTA leaves while its peer can still arrive on its barriers
+    tc_fence_after();
+    if (warp == 1) {
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    }
+}
+
+}  // namespace
+
+size_t gemm_bf16_tc_pair_smem_bytes() { return SMEM_BYTES; }
+
+cudaError_t gemm_bf16_tc_pair_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_b, float* out, const float* bias, int M, int N, int K,
+                                     int num_sms, int* status, cudaStream_t stream) {
+    const int vec_ok = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
+                       (bias == nullptr || (reinterpret_cast<uintptr_t>(bias) & 15u) == 0);
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+        e = cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+        if (e != cudaSuccess) return e;
+        if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+    const int num_tiles = ((M + PBM - 1) / PBM) * ((N + PBN - 1) / PBN);
+    const int max_pairs = num_sms / 2;
+    const int pairs = num_tiles < max_pairs ? num_tiles : max_pairs;
+    gemm_bf16_tc_pair_kernel<<<2 * pairs, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, out, bias, M, N, K, vec_ok, status);
+    return cudaGetLastError();
+}
+
+}  // namespace kg
