@@ -138,7 +138,12 @@ def test_bf16_gemm_picks_tensor_cores_and_simt_for_unaligned(cuda_device):
     a = torch.randn(256, 256, device=cuda_device).bfloat16()
     out = torch.empty(256, 256, device=cuda_device)
     kernels.matmul(out, a, a)
+    assert runtime.last_kernel() == "gemm_bf16_tc_pair_kernel"  # M, N >= 256: CTA-pair tiles
+    small = torch.randn(128, 256, device=cuda_device).bfloat16()
+    out_small = torch.empty(128, 256, device=cuda_device)
+    kernels.matmul(out_small, small, a)
     assert runtime.last_kernel() == "gemm_bf16_tc_kernel"
+    torch.testing.assert_close(out_small, small.float() @ a.float(), rtol=2e-2, atol=2e-2)
     a2 = torch.randn(64, 36, device=cuda_device).bfloat16()  # K % 8 != 0: no TMA row stride
     b2 = torch.randn(36, 48, device=cuda_device).bfloat16()
     out2 = torch.empty(64, 48, device=cuda_device)
