@@ -109,6 +109,20 @@ def build_api_checks() -> Path:
     return API_CHECKS_LIB
 
 
+PIPELINE_CHECKS_SRC = REPO_DIR / "tests" / "cuda_api" / "pipeline_checks.cu"
+PIPELINE_CHECKS_LIB = REPO_DIR / "tests" / "_build" / "libkg_pipeline_checks.so"
+
+
+def build_pipeline_checks() -> Path:
+    """Compile the device checks of the bounded-wait pipeline primitives (tests only)."""
+    deps = [PIPELINE_CHECKS_SRC, CSRC / "kg_ptx.cuh"]
+    if _stale(PIPELINE_CHECKS_LIB, deps):
+        PIPELINE_CHECKS_LIB.parent.mkdir(exist_ok=True)
+        _run([nvcc(), *ARCH_FLAGS, "-O2", "-std=c++17", "-Xcompiler", "-fPIC", "-shared", "-cudart", "static", "-I", str(CSRC),
+              str(PIPELINE_CHECKS_SRC), "-o", str(PIPELINE_CHECKS_LIB)])
+    return PIPELINE_CHECKS_LIB
+
+
 def clean() -> None:
     shutil.rmtree(OBJ_DIR, ignore_errors=True)
     for p in LIB_DIR.glob("*.so"):

@@ -70,8 +70,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 }
 
 // Waits for the phase with the given parity to complete. Returns false (after recording
-// `err` in *status and raising *abort) when the wait gives up or another role aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status, int err) {
+// `err` in *status and raising *abort) when the wait gives up after `timeout_ns`, or at once
+// (without recording) when another role of the CTA already raised *abort.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort, int* status, int err,
+                                              uint64_t timeout_ns) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) {
         return true;
@@ -85,7 +87,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
             if (*abort) {
                 return false;
             }
-            if (globaltimer_ns() - t0 > KG_WAIT_TIMEOUT_NS) {
+            if (globaltimer_ns() - t0 > timeout_ns) {
                 break;
             }
         }
@@ -95,6 +97,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
         atomicCAS(status, 0, err);
     }
     return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status, int err) {
+    return mbar_wait_for(bar, parity, abort, status, err, KG_WAIT_TIMEOUT_NS);
 }
 
 // ---------------------------------------------------------------- TMA (no multicast)
