@@ -38,52 +38,53 @@ __device__ __forceinline__ void store_out<__nv_bfloat16>(__nv_bfloat16* p, float
     *p = __float2bfloat16_rn(v);
 }
 
-// ------------------------------------------------------------------ matmul (64x64 tile, 4x4 per thread)
-constexpr int MM_BM = 64, MM_BN = 64, MM_BK = 16;
-
-template <typename T>
+// ------------------------------------------------------------------ matmul
+// BM x BN output tile per CTA, 256 threads as 16 x 16, each (BM/16) x (BN/16) outputs; K in steps
+// of BK staged in shared memory. Large problems use 64x64x16 tiles; problems with fewer tiles
+// than SMs use 32x32x64 so more CTAs run and each stages more of K per barrier.
+template <typename T, int BM, int BN, int BK>
 __global__ void __launch_bounds__(256) matmul_simt_kernel(float* __restrict__ out, const T* __restrict__ lhs, const T* __restrict__ rhs,
                                                           const float* __restrict__ bias, int M, int N, int K) {
-    __shared__ float sa[MM_BK][MM_BM + 4];
-    __shared__ float sb[MM_BK][MM_BN + 4];
+    constexpr int TM = BM / 16, TN = BN / 16;
+    __shared__ float sa[BK][BM + 4];
+    __shared__ float sb[BK][BN + 4];
     const int tx = threadIdx.x & 15;
     const int ty = threadIdx.x >> 4;
-    const int m0 = blockIdx.y * MM_BM;
-    const int n0 = blockIdx.x * MM_BN;
-    float acc[4][4] = {};
-    for (int k0 = 0; k0 < K; k0 += MM_BK) {
-        for (int i = threadIdx.x; i < MM_BM * MM_BK; i += 256) {
-            const int r = i / MM_BK, c = i % MM_BK;
+    const int m0 = blockIdx.y * BM;
+    const int n0 = blockIdx.x * BN;
+    float acc[TM][TN] = {};
+    for (int k0 = 0; k0 < K; k0 += BK) {
+        for (int i = threadIdx.x; i < BM * BK; i += 256) {
+            const int r = i / BK, c = i % BK;
             const int gm = m0 + r, gk = k0 + c;
             sa[c][r] = (gm < M && gk < K) ? to_f32(lhs[(size_t)gm * K + gk]) : 0.0f;
         }
-        for (int i = threadIdx.x; i < MM_BK * MM_BN; i += 256) {
-            const int r = i / MM_BN, c = i % MM_BN;
+        for (int i = threadIdx.x; i < BK * BN; i += 256) {
+            const int r = i / BN, c = i % BN;
             const int gk = k0 + r, gn = n0 + c;
             sb[r][c] = (gk < K && gn < N) ? to_f32(rhs[(size_t)gk * N + gn]) : 0.0f;
         }
         __syncthreads();
 #pragma unroll
-        for (int kk = 0; kk < MM_BK; ++kk) {
-            float a[4], b[4];
+        for (int kk = 0; kk < BK; ++kk) {
+            float a[TM], b[TN];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                a[i] = sa[kk][ty + 16 * i];
-                b[i] = sb[kk][tx + 16 * i];
-            }
+            for (int i = 0; i < TM; ++i) a[i] = sa[kk][ty + 16 * i];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int j = 0; j < TN; ++j) b[j] = sb[kk][tx + 16 * j];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < TM; ++i) {
         const int gm = m0 + ty + 16 * i;
         if (gm >= M) continue;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < TN; ++j) {
             const int gn = n0 + tx + 16 * j;
             if (gn < N) {
                 out[(size_t)gm * N + gn] = acc[i][j] + (bias ? bias[gn] : 0.0f);
@@ -95,20 +96,21 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(float* __restrict__ ou
 // ------------------------------------------------------------------ conv2d implicit GEMM
 // GEMM rows = output channels f, columns = (b, ho, wo), reduction = (c, kh, kw) in the
 // reference's weight2 / col2 order (OIHW flattening).
-constexpr int CV_BM = 32, CV_BN = 64, CV_BK = 16;
-
-template <typename T>
+// CV_BM output channels x CV_BN output pixels per CTA; 256 threads as 8 (channels) x 32 (pixels),
+// each (CV_BM/8) x (CV_BN/32) outputs. Small problems use 16 x 32 tiles with K steps of 48.
+template <typename T, int CV_BM, int CV_BN, int CV_BK>
 __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ out, const T* __restrict__ input, const T* __restrict__ weight,
                                                           const float* __restrict__ bias, Conv2dShape s) {
+    constexpr int TM = CV_BM / 8, TN = CV_BN / 32;
     __shared__ float sw[CV_BK][CV_BM + 1];
     __shared__ float sx[CV_BK][CV_BN + 4];
     const int Kred = s.C * s.KH * s.KW;
     const long long Ncols = (long long)s.B * s.HO * s.WO;
     const int f0 = blockIdx.y * CV_BM;
     const long long n0 = (long long)blockIdx.x * CV_BN;
-    const int tx = threadIdx.x & 31;  // columns tx, tx+32
-    const int ty = threadIdx.x >> 5;  // rows ty, ty+8, ty+16, ty+24
-    float acc[4][2] = {};
+    const int tx = threadIdx.x & 31;  // columns tx + 32 j
+    const int ty = threadIdx.x >> 5;  // rows ty + 8 i
+    float acc[TM][TN] = {};
     for (int k0 = 0; k0 < Kred; k0 += CV_BK) {
         for (int i = threadIdx.x; i < CV_BM * CV_BK; i += 256) {
             const int r = i / CV_BK, c = i % CV_BK;
@@ -140,25 +142,24 @@ __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ ou
         __syncthreads();
 #pragma unroll
         for (int kk = 0; kk < CV_BK; ++kk) {
-            float a[4], x[2];
+            float a[TM], x[TN];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) a[i] = sw[kk][ty + 8 * i];
-            x[0] = sx[kk][tx];
-            x[1] = sx[kk][tx + 32];
+            for (int i = 0; i < TM; ++i) a[i] = sw[kk][ty + 8 * i];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                acc[i][0] = fmaf(a[i], x[0], acc[i][0]);
-                acc[i][1] = fmaf(a[i], x[1], acc[i][1]);
-            }
+            for (int j = 0; j < TN; ++j) x[j] = sx[kk][tx + 32 * j];
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+#pragma unroll
+                for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], x[j], acc[i][j]);
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < TM; ++i) {
         const int f = f0 + ty + 8 * i;
         if (f >= s.F) continue;
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
+        for (int j = 0; j < TN; ++j) {
             const long long col = n0 + tx + 32 * j;
             if (col >= Ncols) continue;
             const int b = (int)(col / ((long long)s.HO * s.WO));
@@ -169,13 +170,14 @@ __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ ou
 }
 
 // ------------------------------------------------------------------ flash attention
-// One CTA = 64 query rows of one (b, h); 256 threads = 64 rows x 4 threads. Key/value tiles of
-// 64 rows are staged in shared memory as f32. Thread (r, t) scores keys t, t+4, ..., owns
+// One CTA = FA_BR query rows of one (b, h), 4 threads per row. Key/value tiles of 64 rows are
+// staged in shared memory as f32. Thread (r, t) scores keys t, t+4, ..., owns
 // output columns t, t+4, ...; the row's max / sum are combined with two xor shuffles.
-constexpr int FA_BR = 64, FA_BC = 64, FA_MAX_D = 128;
+constexpr int FA_BC = 64, FA_MAX_D = 128;
 
-template <typename T>
-__global__ void __launch_bounds__(256) flash_attn_simt_kernel(T* __restrict__ out, const T* __restrict__ q, const T* __restrict__ k,
+// FA_BR query rows per CTA, 4 threads per row (FA_BR * 4 threads).
+template <typename T, int FA_BR>
+__global__ void __launch_bounds__(FA_BR * 4) flash_attn_simt_kernel(T* __restrict__ out, const T* __restrict__ q, const T* __restrict__ k,
                                                               const T* __restrict__ v, int H, int S, int D, float scale_log2, int causal) {
     extern __shared__ float fa_smem[];
     const int dpad = D + 1;
@@ -190,7 +192,7 @@ __global__ void __launch_bounds__(256) flash_attn_simt_kernel(T* __restrict__ ou
     const int t = threadIdx.x & 3;
     const int row = m0 + r;
 
-    for (int i = threadIdx.x; i < FA_BR * D; i += 256) {
+    for (int i = threadIdx.x; i < FA_BR * D; i += FA_BR * 4) {
         const int rr = i / D, d = i - rr * D;
         sq[rr * dpad + d] = (m0 + rr < S) ? to_f32(q[base + (size_t)(m0 + rr) * D + d]) : 0.0f;
     }
@@ -201,7 +203,7 @@ __global__ void __launch_bounds__(256) flash_attn_simt_kernel(T* __restrict__ ou
     const int n_end = causal ? min(S, m0 + FA_BR) : S;
     for (int n0 = 0; n0 < n_end; n0 += FA_BC) {
         __syncthreads();
-        for (int i = threadIdx.x; i < FA_BC * D; i += 256) {
+        for (int i = threadIdx.x; i < FA_BC * D; i += FA_BR * 4) {
             const int j = i / D, d = i - j * D;
             const bool ok = n0 + j < S;
             sk[j * dpad + d] = ok ? to_f32(k[base + (size_t)(n0 + j) * D + d]) : 0.0f;
@@ -262,8 +264,14 @@ __global__ void __launch_bounds__(256) flash_attn_simt_kernel(T* __restrict__ ou
 
 template <typename T>
 cudaError_t matmul_simt_launch(float* out, const T* lhs, const T* rhs, const float* bias, int M, int N, int K, cudaStream_t stream) {
-    dim3 grid((N + MM_BN - 1) / MM_BN, (M + MM_BM - 1) / MM_BM);
-    matmul_simt_kernel<T><<<grid, 256, 0, stream>>>(out, lhs, rhs, bias, M, N, K);
+    const long long big_tiles = (long long)((N + 63) / 64) * ((M + 63) / 64);
+    if (big_tiles >= 148) {
+        dim3 grid((N + 63) / 64, (M + 63) / 64);
+        matmul_simt_kernel<T, 64, 64, 16><<<grid, 256, 0, stream>>>(out, lhs, rhs, bias, M, N, K);
+    } else {
+        dim3 grid((N + 31) / 32, (M + 31) / 32);
+        matmul_simt_kernel<T, 32, 32, 64><<<grid, 256, 0, stream>>>(out, lhs, rhs, bias, M, N, K);
+    }
     return cudaGetLastError();
 }
 template cudaError_t matmul_simt_launch<float>(float*, const float*, const float*, const float*, int, int, int, cudaStream_t);
@@ -274,13 +282,31 @@ template <typename T>
 cudaError_t conv2d_simt_launch(float* out, const T* input, const T* weight, const float* bias, const Conv2dShape& s,
                                cudaStream_t stream) {
     const long long ncols = (long long)s.B * s.HO * s.WO;
-    dim3 grid((unsigned)((ncols + CV_BN - 1) / CV_BN), (s.F + CV_BM - 1) / CV_BM);
-    conv2d_simt_kernel<T><<<grid, 256, 0, stream>>>(out, input, weight, bias, s);
+    const long long big_tiles = ((ncols + 63) / 64) * ((s.F + 31) / 32);
+    if (big_tiles >= 148) {
+        dim3 grid((unsigned)((ncols + 63) / 64), (s.F + 31) / 32);
+        conv2d_simt_kernel<T, 32, 64, 16><<<grid, 256, 0, stream>>>(out, input, weight, bias, s);
+    } else {
+        dim3 grid((unsigned)((ncols + 31) / 32), (s.F + 15) / 16);
+        conv2d_simt_kernel<T, 16, 32, 48><<<grid, 256, 0, stream>>>(out, input, weight, bias, s);
+    }
     return cudaGetLastError();
 }
 template cudaError_t conv2d_simt_launch<float>(float*, const float*, const float*, const float*, const Conv2dShape&, cudaStream_t);
 template cudaError_t conv2d_simt_launch<__nv_bfloat16>(float*, const __nv_bfloat16*, const __nv_bfloat16*, const float*,
                                                        const Conv2dShape&, cudaStream_t);
+
+template <typename T, int BR>
+static cudaError_t flash_attn_simt_launch_br(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
+                                             cudaStream_t stream) {
+    const size_t smem = sizeof(float) * ((size_t)BR * (D + 1) + (size_t)FA_BC * (D + 1) + (size_t)FA_BC * D + BR * (FA_BC + 1));
+    cudaError_t e = cudaFuncSetAttribute(flash_attn_simt_kernel<T, BR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((S + BR - 1) / BR, B * H);
+    const float scale_log2 = scale * 1.4426950408889634f;  // scores in the exp2 domain
+    flash_attn_simt_kernel<T, BR><<<grid, BR * 4, smem, stream>>>(out, q, k, v, H, S, D, scale_log2, causal);
+    return cudaGetLastError();
+}
 
 template <typename T>
 cudaError_t flash_attn_simt_launch(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
@@ -288,13 +314,11 @@ cudaError_t flash_attn_simt_launch(T* out, const T* q, const T* k, const T* v, i
     if (D > FA_MAX_D) {
         return cudaErrorInvalidValue;
     }
-    const size_t smem = sizeof(float) * ((size_t)FA_BR * (D + 1) + (size_t)FA_BC * (D + 1) + (size_t)FA_BC * D + FA_BR * (FA_BC + 1));
-    cudaError_t e = cudaFuncSetAttribute(flash_attn_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    dim3 grid((S + FA_BR - 1) / FA_BR, B * H);
-    const float scale_log2 = scale * 1.4426950408889634f;  // scores in the exp2 domain
-    flash_attn_simt_kernel<T><<<grid, 256, smem, stream>>>(out, q, k, v, H, S, D, scale_log2, causal);
-    return cudaGetLastError();
+    // Few (b, h, query-block) units: 16-row blocks so that at least two CTAs per SM have work.
+    if ((long long)B * H * ((S + 63) / 64) < 2 * 148) {
+        return flash_attn_simt_launch_br<T, 16>(out, q, k, v, B, H, S, D, scale, causal, stream);
+    }
+    return flash_attn_simt_launch_br<T, 64>(out, q, k, v, B, H, S, D, scale, causal, stream);
 }
 template cudaError_t flash_attn_simt_launch<float>(float*, const float*, const float*, const float*, int, int, int, int, float, int,
                                                    cudaStream_t);
