@@ -314,10 +314,6 @@ cudaError_t flash_attn_simt_launch(T* out, const T* q, const T* k, const T* v, i
     if (D > FA_MAX_D) {
         return cudaErrorInvalidValue;
     }
-    // Few (b, h, query-block) units: 16-row blocks so that at least two CTAs per SM have work.
-    if ((long long)B * H * ((S + 63) / 64) < 2 * 148) {
-        return flash_attn_simt_launch_br<T, 16>(out, q, k, v, B, H, S, D, scale, causal, stream);
-    }
     return flash_attn_simt_launch_br<T, 64>(out, q, k, v, B, H, S, D, scale, causal, stream);
 }
 template cudaError_t flash_attn_simt_launch<float>(float*, const float*, const float*, const float*, int, int, int, int, float, int,
