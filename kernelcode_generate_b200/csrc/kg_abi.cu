@@ -13,6 +13,7 @@
 #include <vector>
 
 #include "../../include/kg_sm100.h"
+#include "kg_conv_tc.h"
 #include "kg_flash_tc.h"
 #include "kg_gemm_tc.h"
 #include "kg_simt.h"
@@ -119,6 +120,45 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long rows, long l
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// N-d bf16 tensor map (dims innermost first, byte strides of dims 1..rank-1), 128B swizzle.
+int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box) {
+    EncodeTiledFn encode = nullptr;
+    int rc = get_encode_fn(&encode);
+    if (rc != KG_OK) return rc;
+    cuuint32_t estrides[5] = {1, 1, 1, 1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), dims, strides, box, estrides,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(KG_ERR_CUDA, "cuTensorMapEncodeTiled (%d-D) failed (%d)", rank, static_cast<int>(r));
+    return KG_OK;
+}
+
+// Per-device scratch for kernels that repack their operands (grow-only, reused across calls).
+struct Scratch {
+    void* ptr = nullptr;
+    size_t cap = 0;
+};
+std::vector<Scratch> g_scratch;
+
+int device_scratch(size_t bytes, void** out) {
+    int dev = 0;
+    KG_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (static_cast<int>(g_scratch.size()) <= dev) g_scratch.resize(dev + 1);
+    Scratch& sc = g_scratch[dev];
+    if (sc.cap < bytes) {
+        // The previous buffer may still be read by kernels in flight on any stream.
+        KG_CUDA_TRY(cudaDeviceSynchronize());
+        if (sc.ptr) KG_CUDA_TRY(cudaFree(sc.ptr));
+        sc.ptr = nullptr;
+        sc.cap = 0;
+        KG_CUDA_TRY(cudaMalloc(&sc.ptr, bytes));
+        sc.cap = bytes;
+    }
+    *out = sc.ptr;
+    return KG_OK;
+}
+
 // 3-D bf16 tensor map over a contiguous [BH, S, D] tensor (dims {D, S, BH}), box {64, box_rows, 1}, 128B swizzle.
 int make_tmap_3d_bf16(CUtensorMap* map, const void* base, long long BH, long long S, long long D, int box_rows) {
     EncodeTiledFn encode = nullptr;
@@ -185,6 +225,35 @@ int conv2d_impl(float* out, const void* input, const void* weight, int in_dtype,
         return KG_OK;
     }
     if (in_dtype == KG_DTYPE_BF16) {
+        kg::ConvTcShape t{s.B, s.C, (s.C + 7) / 8 * 8, s.XH, s.XW, s.F, s.KH, s.KW, s.HO, s.WO, s.sh, s.sw, s.dh, s.dw,
+                          s.pt, s.pb, s.pl, s.pr, 0, 0};
+        t.tile_w = t.WO < 128 ? t.WO : 128;
+        t.rows = 128 / t.tile_w < t.HO ? 128 / t.tile_w : t.HO;
+        if (kg::conv2d_tc_supported(t) && aligned16(out)) {
+            DeviceInfo* dev = nullptr;
+            int rc = device_info(&dev);
+            if (rc != KG_OK) return rc;
+            const size_t x_elems = static_cast<size_t>(t.B) * t.XH * t.XW * t.Cp;
+            const size_t w_elems = static_cast<size_t>(t.F) * t.KH * t.KW * t.Cp;
+            const size_t x_bytes = (x_elems * 2 + 255) & ~size_t(255);
+            void* scratch = nullptr;
+            if ((rc = device_scratch(x_bytes + w_elems * 2, &scratch))) return rc;
+            __nv_bfloat16* x_nhwc = static_cast<__nv_bfloat16*>(scratch);
+            __nv_bfloat16* w_ftc = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(scratch) + x_bytes);
+            KG_CUDA_TRY(kg::conv2d_tc_repack(x_nhwc, w_ftc, static_cast<const __nv_bfloat16*>(input),
+                                             static_cast<const __nv_bfloat16*>(weight), t, stream));
+            CUtensorMap tx, tw;
+            const cuuint64_t xd[4] = {(cuuint64_t)t.Cp, (cuuint64_t)t.XW, (cuuint64_t)t.XH, (cuuint64_t)t.B};
+            const cuuint64_t xs[3] = {(cuuint64_t)t.Cp * 2, (cuuint64_t)t.XW * t.Cp * 2, (cuuint64_t)t.XH * t.XW * t.Cp * 2};
+            const cuuint32_t xb[4] = {64, (cuuint32_t)t.tile_w, (cuuint32_t)t.rows, 1};
+            const cuuint64_t wd[3] = {(cuuint64_t)t.Cp, (cuuint64_t)(t.KH * t.KW), (cuuint64_t)t.F};
+            const cuuint64_t ws[2] = {(cuuint64_t)t.Cp * 2, (cuuint64_t)t.KH * t.KW * t.Cp * 2};
+            const cuuint32_t wb[3] = {64, 1, (cuuint32_t)kg::conv2d_tc_block_n(t.F)};
+            if ((rc = make_tmap_bf16(&tx, x_nhwc, 4, xd, xs, xb)) || (rc = make_tmap_bf16(&tw, w_ftc, 3, wd, ws, wb))) return rc;
+            g_last_kernel = "conv2d_tc_kernel";
+            KG_CUDA_TRY(kg::conv2d_tc_launch(tx, tw, out, bias, t, dev->status, stream));
+            return KG_OK;
+        }
         g_last_kernel = "conv2d_simt_kernel<bf16>";
         KG_CUDA_TRY(kg::conv2d_simt_launch(out, static_cast<const __nv_bfloat16*>(input), static_cast<const __nv_bfloat16*>(weight),
                                            bias, s, stream));

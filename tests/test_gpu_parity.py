@@ -269,3 +269,40 @@ def test_typed_entries_report_errors_without_launching(cuda_device):
         runtime.check(runtime.load().kg_sm100_matmul(x.data_ptr(), x.data_ptr(), x.data_ptr(), 1, None, 0, 4, 4, None))
     assert e.value.code == runtime.KG_ERR_INVALID_ARGUMENT
     assert runtime.device_status() == 0
+
+
+# ---------------------------------------------------------------- bf16 conv2d on tensor cores
+@pytest.mark.parametrize("x_shape,f,k,stride,dilation,pads,with_bias", [
+    ((1, 16, 32, 32), 32, (3, 3), (1, 1), (1, 1), (1, 1, 1, 1), False),      # C2's shape in bf16
+    ((2, 64, 28, 28), 128, (3, 3), (1, 1), (1, 1), (1, 1, 1, 1), True),
+    ((1, 3, 20, 30), 8, (5, 5), (1, 1), (2, 1), (2, 1, 0, 3), True),          # C % 8 != 0, dilation, asymmetric pads
+    ((2, 72, 9, 200), 40, (3, 1), (1, 1), (1, 1), (0, 0, 0, 0), False),        # WO > 128: several tiles per row
+    ((1, 8, 10, 12), 200, (1, 1), (1, 1), (1, 1), (0, 0, 0, 0), True),         # F > 128: several column tiles
+])
+def test_bf16_conv2d_tensor_cores_vs_oracle(cuda_device, x_shape, f, k, stride, dilation, pads, with_bias):
+    torch = _torch()
+    rng = np.random.default_rng(sum(x_shape) + f)
+    x = workloads.bf16_bits(rng.uniform(-1, 1, x_shape).astype(np.float32))
+    w = workloads.bf16_bits((rng.standard_normal((f, x_shape[1], *k), dtype=np.float32) / np.float32(np.sqrt(x_shape[1] * k[0] * k[1]))))
+    bias = rng.standard_normal(f, dtype=np.float32) if with_bias else None
+    expect = oracle.conv2d(x, w, bias, stride=stride, dilation=dilation, pads=pads, tiles=(8, 16, 4, 8, 9))
+    out = torch.full(expect.shape, float("nan"), device=cuda_device)
+    kernels.conv2d(out, _to_torch(x, cuda_device), _to_torch(w, cuda_device), None if bias is None else _to_torch(bias, cuda_device),
+                   stride, dilation, pads)
+    torch.cuda.synchronize()
+    assert runtime.last_kernel() == "conv2d_tc_kernel"
+    assert runtime.device_status() == 0
+    np.testing.assert_allclose(out.cpu().numpy(), expect, **BF16_TOL)
+
+
+def test_bf16_conv2d_strided_uses_cuda_cores(cuda_device):
+    torch = _torch()
+    rng = np.random.default_rng(5)
+    x = workloads.bf16_bits(rng.uniform(-1, 1, (1, 8, 17, 19)).astype(np.float32))
+    w = workloads.bf16_bits(rng.standard_normal((12, 8, 3, 3), dtype=np.float32) / np.float32(8.0))
+    expect = oracle.conv2d(x, w, None, stride=(2, 2), dilation=(1, 1), pads=(1, 1, 1, 1), tiles=(8, 16, 4, 8, 9))
+    out = torch.empty(expect.shape, device=cuda_device)
+    kernels.conv2d(out, _to_torch(x, cuda_device), _to_torch(w, cuda_device), None, (2, 2), (1, 1), (1, 1, 1, 1))
+    torch.cuda.synchronize()
+    assert runtime.last_kernel() == "conv2d_simt_kernel<bf16>"
+    np.testing.assert_allclose(out.cpu().numpy(), expect, **BF16_TOL)
