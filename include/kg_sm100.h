@@ -110,6 +110,28 @@ KG_API int kg_sm100_flash_attention(void* out, const void* q, const void* k, con
                              long long B, long long H, long long S, long long D, float scale, int causal,
                              void* stream);
 
+/* Tensor-core conv2d that allocates nothing. No counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc (a serving process whose memory pool already owns the
+ * device's free memory, a runtime that forbids allocation after start-up, a fixed device-memory
+ * budget): same arguments and result as kg_sm100_conv2d on its bf16 tensor-core path (stride 1),
+ * but the NHWC repack scratch lives in a fixed array of KG_CONV2D_NOALLOC_SCRATCH_BYTES inside the
+ * library, which every device that loads the library holds until the process exits. No
+ * cudaMalloc, cudaFree or other allocating routine is called.
+ *  - The first call on each device looks up the array's device address (with that device
+ *    current); make that first call before any stream capture.
+ *  - Inputs needing more scratch than the array holds (B*XH*XW*Cp*2 rounded up to 256 bytes plus
+ *    F*KH*KW*Cp*2, Cp = C rounded up to a multiple of 8), f32 inputs and strides other than 1
+ *    return KG_ERR_UNSUPPORTED with a message.
+ *  - All calls share the array; each call rewrites every element it reads, so nothing left by a
+ *    previous call leaks into a result, but calls that overlap on the GPU (other streams, other
+ *    host threads) race on it: order them on one stream. */
+#define KG_CONV2D_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+KG_API int kg_sm100_conv2d_noalloc(float* out, const void* input, const void* weight, int in_dtype, const float* bias,
+                                   long long B, long long C, long long XH, long long XW, long long F, long long KH, long long KW,
+                                   long long stride_h, long long stride_w, long long dilation_h, long long dilation_w,
+                                   long long pad_top, long long pad_bottom, long long pad_left, long long pad_right, void* stream);
+
 /* Synchronises the current device, returns its device status word (0 = no kernel reported a
  * pipeline timeout since the last call) in *code and clears it. */
 KG_API int kg_sm100_device_status(int* code);

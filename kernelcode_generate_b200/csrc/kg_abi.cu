@@ -580,3 +580,83 @@ int kg_sm100_flash_attention_entry(const KgArgSlot* slots, unsigned long long n)
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- conv2d without allocation
+//
+// Some callers cannot call cudaMalloc: a serving process whose memory pool already owns the
+// device's free memory (an extra cudaMalloc there fails or fragments the pool), a runtime that
+// forbids device allocation after start-up so that latency stays predictable, or a host that
+// runs under a fixed device-memory budget. kg_sm100_conv2d gets its repack scratch from a
+// cached cudaMalloc; kg_sm100_conv2d_noalloc runs the same tensor-core conv2d with its scratch in
+// the fixed array below, which the library's module holds on every device it is loaded on until
+// the process exits. It calls no cudaMalloc, cudaFree or other allocating routine.
+namespace {
+
+__device__ __align__(256) static unsigned char kg_conv2d_noalloc_scratch[KG_CONV2D_NOALLOC_SCRATCH_BYTES];
+
+// Device address of the array, looked up once per device with that device current (host code may
+// not use the symbol itself: on the host it names a stand-in, not device memory).
+std::mutex g_noalloc_mu;
+void* g_noalloc_scratch_ptr[64] = {};
+
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    KG_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(KG_ERR_UNSUPPORTED, "conv2d_noalloc: device ordinal %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_scratch_ptr[dev] == nullptr) {
+        void* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, kg_conv2d_noalloc_scratch);
+        if (e != cudaSuccess || ptr == nullptr) return cuda_fail(e, "cudaGetSymbolAddress(kg_conv2d_noalloc_scratch)");
+        g_noalloc_scratch_ptr[dev] = ptr;
+    }
+    *out = g_noalloc_scratch_ptr[dev];
+    return KG_OK;
+}
+
+}  // namespace
+
+extern "C" int kg_sm100_conv2d_noalloc(float* out, const void* input, const void* weight, int in_dtype, const float* bias, long long B,
+                                       long long C, long long XH, long long XW, long long F, long long KH, long long KW, long long stride_h,
+                                       long long stride_w, long long dilation_h, long long dilation_w, long long pad_top,
+                                       long long pad_bottom, long long pad_left, long long pad_right, void* stream) {
+    if (!out || !input || !weight) return fail(KG_ERR_INVALID_ARGUMENT, "conv2d_noalloc: null pointer");
+    if (in_dtype != KG_DTYPE_BF16) return fail(KG_ERR_UNSUPPORTED, "conv2d_noalloc: bf16 inputs only (dtype code %d)", in_dtype);
+    kg::Conv2dShape s;
+    int rc = conv2d_shape(&s, B, C, XH, XW, F, KH, KW, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_bottom, pad_left,
+                          pad_right);
+    if (rc != KG_OK) return rc;
+    kg::ConvTcShape t{s.B, s.C, (s.C + 7) / 8 * 8, s.XH, s.XW, s.F, s.KH, s.KW, s.HO, s.WO, s.sh, s.sw, s.dh, s.dw,
+                      s.pt, s.pb, s.pl, s.pr, 0, 0};
+    t.tile_w = t.WO < 128 ? t.WO : 128;
+    t.rows = 128 / t.tile_w < t.HO ? 128 / t.tile_w : t.HO;
+    if (!kg::conv2d_tc_supported(t) || !aligned16(out))
+        return fail(KG_ERR_UNSUPPORTED, "conv2d_noalloc: only the tensor-core path (stride 1, 16-byte aligned out)");
+    const size_t x_bytes = (static_cast<size_t>(t.B) * t.XH * t.XW * t.Cp * 2 + 255) & ~size_t(255);
+    const size_t need = x_bytes + static_cast<size_t>(t.F) * t.KH * t.KW * t.Cp * 2;
+    if (need > KG_CONV2D_NOALLOC_SCRATCH_BYTES)
+        return fail(KG_ERR_UNSUPPORTED, "conv2d_noalloc: needs %zu bytes of scratch, the fixed array holds %zu", need,
+                    static_cast<size_t>(KG_CONV2D_NOALLOC_SCRATCH_BYTES));
+    DeviceInfo* dev = nullptr;
+    if ((rc = device_info(&dev))) return rc;
+    void* scratch = nullptr;
+    if ((rc = noalloc_scratch(&scratch))) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    __nv_bfloat16* x_nhwc = static_cast<__nv_bfloat16*>(scratch);
+    __nv_bfloat16* w_ftc = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(scratch) + x_bytes);
+    // The repack writes every element the conv kernel reads (channel padding included), so the
+    // previous call's contents need no clearing.
+    KG_CUDA_TRY(kg::conv2d_tc_repack(x_nhwc, w_ftc, static_cast<const __nv_bfloat16*>(input), static_cast<const __nv_bfloat16*>(weight), t,
+                                     st));
+    CUtensorMap tx, tw;
+    const cuuint64_t xd[4] = {(cuuint64_t)t.Cp, (cuuint64_t)t.XW, (cuuint64_t)t.XH, (cuuint64_t)t.B};
+    const cuuint64_t xs[3] = {(cuuint64_t)t.Cp * 2, (cuuint64_t)t.XW * t.Cp * 2, (cuuint64_t)t.XH * t.XW * t.Cp * 2};
+    const cuuint32_t xb[4] = {64, (cuuint32_t)t.tile_w, (cuuint32_t)t.rows, 1};
+    const cuuint64_t wd[3] = {(cuuint64_t)t.Cp, (cuuint64_t)(t.KH * t.KW), (cuuint64_t)t.F};
+    const cuuint64_t ws[2] = {(cuuint64_t)t.Cp * 2, (cuuint64_t)t.KH * t.KW * t.Cp * 2};
+    const cuuint32_t wb[3] = {64, 1, (cuuint32_t)kg::conv2d_tc_block_n(t.F)};
+    if ((rc = make_tmap_bf16(&tx, x_nhwc, 4, xd, xs, xb)) || (rc = make_tmap_bf16(&tw, w_ftc, 3, wd, ws, wb))) return rc;
+    g_last_kernel = "conv2d_tc_kernel";
+    KG_CUDA_TRY(kg::conv2d_tc_launch(tx, tw, out, bias, t, dev->status, st));
+    return KG_OK;
+}
