@@ -129,7 +129,7 @@ template <int D>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, __nv_bfloat16* __restrict__ out, int S, float scale_log2,
-                        int causal, int num_pairs, int* status) {
+                        int causal, int num_pairs, int BH, int group_heads, int* status) {
     using Cfg = FlashCfg<D>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -149,10 +149,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    // x walks the query-tile pairs of one (b, h) so co-resident CTAs share that head's K/V in L2;
-    // within a head the heaviest (latest, for causal) pairs start first.
-    const int bh = blockIdx.y;
-    const int pair = num_pairs - 1 - static_cast<int>(blockIdx.x);
+    // CTAs are dispatched in groups of `group_heads` heads. Within a group the heaviest query-tile
+    // pairs (the latest, for causal) of every head start first, so the light ones fill the tail;
+    // a group's K/V is sized to stay in L2 while its CTAs run.
+    const int per_group = group_heads * num_pairs;
+    const int linear = static_cast<int>(blockIdx.x);
+    const int group = linear / per_group;
+    const int r = linear - group * per_group;
+    const int h0 = group * group_heads;
+    const int gh = min(group_heads, BH - h0);
+    const int bh = h0 + r % gh;
+    const int pair = num_pairs - 1 - r / gh;
     const int m0 = pair * 2 * BM;
     const int n_tiles0 = key_tiles_for(m0, S, causal);
     const int n_tiles1 = (m0 + BM < S) ? key_tiles_for(m0 + BM, S, causal) : 0;
@@ -435,7 +442,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }  // namespace
 
 bool flash_fwd_tc_supported(long long B, long long H, long long S, long long D) {
-    return (D == 64 || D == 128) && S > 0 && S < (1LL << 30) && B * H > 0 && B * H < 65536;
+    const long long pairs = (S + 2 * BM - 1) / (2 * BM);
+    return (D == 64 || D == 128) && S > 0 && S < (1LL << 30) && B * H > 0 && B * H < 65536 && pairs * B * H < (1LL << 31);
+}
+
+// Heads per dispatch group: a power of two whose K/V (2 * S * D bf16 per head) fits in 64 MiB of L2.
+static int flash_group_heads(int BH, int S, int D) {
+    const long long kv_head_bytes = 4LL * S * D;
+    long long cap = (64LL << 20) / (kv_head_bytes > 0 ? kv_head_bytes : 1);
+    if (cap > BH) cap = BH;
+    int g = 1;
+    while (2LL * g <= cap) g *= 2;
+    return g;
 }
 
 size_t flash_fwd_tc_smem_bytes(int D) { return D == 64 ? FlashCfg<64>::SMEM_BYTES : FlashCfg<128>::SMEM_BYTES; }
@@ -444,7 +462,8 @@ cudaError_t flash_fwd_tc_launch(const CUtensorMap& tm_q, const CUtensorMap& tm_k
                                 int BH, int S, int D, float scale, int causal, int* status, cudaStream_t stream) {
     const int num_pairs = (S + 2 * BM - 1) / (2 * BM);
     const float scale_log2 = scale * 1.4426950408889634f;
-    dim3 grid(num_pairs, BH);
+    const int group_heads = flash_group_heads(BH, S, D);
+    dim3 grid(static_cast<unsigned>(num_pairs) * static_cast<unsigned>(BH));
     static bool attr_set[2][64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -460,10 +479,10 @@ cudaError_t flash_fwd_tc_launch(const CUtensorMap& tm_q, const CUtensorMap& tm_k
     }
     if (D == 64) {
         flash_fwd_tc_kernel<64><<<grid, NUM_THREADS, FlashCfg<64>::SMEM_BYTES, stream>>>(tm_q, tm_k, tm_v, out, S, scale_log2, causal,
-                                                                                         num_pairs, status);
+                                                                                         num_pairs, BH, group_heads, status);
     } else if (D == 128) {
         flash_fwd_tc_kernel<128><<<grid, NUM_THREADS, FlashCfg<128>::SMEM_BYTES, stream>>>(tm_q, tm_k, tm_v, out, S, scale_log2,
-                                                                                           causal, num_pairs, status);
+                                                                                           causal, num_pairs, BH, group_heads, status);
     } else {
         return cudaErrorInvalidValue;
     }

@@ -170,92 +170,121 @@ __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ ou
 }
 
 // ------------------------------------------------------------------ flash attention
-// One CTA = FA_BR query rows of one (b, h), 4 threads per row. Key/value tiles of 64 rows are
-// staged in shared memory as f32. Thread (r, t) scores keys t, t+4, ..., owns
-// output columns t, t+4, ...; the row's max / sum are combined with two xor shuffles.
-constexpr int FA_BC = 64, FA_MAX_D = 128;
+// One CTA = 64 query rows of one (b, h); 256 threads as 16 x 16 (ty, tx). Key/value tiles of 64
+// rows. Thread (ty, tx) owns scores rows 4ty..4ty+3 x keys 4tx..4tx+3 and output rows 4ty..4ty+3 x
+// head columns tx, tx+16, ... (DT of them, D padded to 16*DT). Q and K are staged transposed
+// ([d][row]) so each step of Q.K^T is two float4 shared loads for 16 FMAs; P goes through shared
+// memory to the P.V product. Row max / sum combine over the 16 tx threads of a row with shuffles.
+constexpr int FA_BR = 64, FA_BC = 64;
 
-// FA_BR query rows per CTA, 4 threads per row (FA_BR * 4 threads).
-template <typename T, int FA_BR>
-__global__ void __launch_bounds__(FA_BR * 4) flash_attn_simt_kernel(T* __restrict__ out, const T* __restrict__ q, const T* __restrict__ k,
+template <typename T, int DT>
+__global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__ out, const T* __restrict__ q, const T* __restrict__ k,
                                                               const T* __restrict__ v, int H, int S, int D, float scale_log2, int causal) {
-    extern __shared__ float fa_smem[];
-    const int dpad = D + 1;
-    float* sq = fa_smem;                  // [FA_BR][D+1]
-    float* sk = sq + FA_BR * dpad;        // [FA_BC][D+1]
-    float* sv = sk + FA_BC * dpad;        // [FA_BC][D]
-    float* sp = sv + FA_BC * D;           // [FA_BR][FA_BC+1]
+    constexpr int DP = 16 * DT;          // padded head dim
+    constexpr int LDT = FA_BR + 4;       // row pitch of the transposed tiles
+    extern __shared__ float4 fa_smem4[];
+    float* fa_smem = reinterpret_cast<float*>(fa_smem4);
+    float* sQt = fa_smem;                // [DP][LDT]
+    float* sKt = sQt + DP * LDT;         // [DP][LDT]
+    float* sV = sKt + DP * LDT;          // [FA_BC][DP + 4]
+    float* sP = sV + FA_BC * (DP + 4);   // [FA_BR][FA_BC + 4]
     const int bh = blockIdx.y;
     const int m0 = blockIdx.x * FA_BR;
     const size_t base = (size_t)bh * S * D;
-    const int r = threadIdx.x >> 2;
-    const int t = threadIdx.x & 3;
-    const int row = m0 + r;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
 
-    for (int i = threadIdx.x; i < FA_BR * D; i += FA_BR * 4) {
-        const int rr = i / D, d = i - rr * D;
-        sq[rr * dpad + d] = (m0 + rr < S) ? to_f32(q[base + (size_t)(m0 + rr) * D + d]) : 0.0f;
+    for (int i = threadIdx.x; i < FA_BR * DP; i += 256) {
+        const int r = i / DP, d = i - r * DP;
+        sQt[d * LDT + r] = (m0 + r < S && d < D) ? to_f32(q[base + (size_t)(m0 + r) * D + d]) : 0.0f;
     }
-    float o[FA_MAX_D / 4];
+    float o[4][DT];
+    float m_run[4], l_run[4];
 #pragma unroll
-    for (int i = 0; i < FA_MAX_D / 4; ++i) o[i] = 0.0f;
-    float m_run = -INFINITY, l_run = 0.0f;
+    for (int a = 0; a < 4; ++a) {
+        m_run[a] = -INFINITY;
+        l_run[a] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < DT; ++c) o[a][c] = 0.0f;
+    }
     const int n_end = causal ? min(S, m0 + FA_BR) : S;
     for (int n0 = 0; n0 < n_end; n0 += FA_BC) {
         __syncthreads();
-        for (int i = threadIdx.x; i < FA_BC * D; i += FA_BR * 4) {
-            const int j = i / D, d = i - j * D;
-            const bool ok = n0 + j < S;
-            sk[j * dpad + d] = ok ? to_f32(k[base + (size_t)(n0 + j) * D + d]) : 0.0f;
-            sv[j * D + d] = ok ? to_f32(v[base + (size_t)(n0 + j) * D + d]) : 0.0f;
+        for (int i = threadIdx.x; i < FA_BC * DP; i += 256) {
+            const int j = i / DP, d = i - j * DP;
+            const bool ok = n0 + j < S && d < D;
+            sKt[d * LDT + j] = ok ? to_f32(k[base + (size_t)(n0 + j) * D + d]) : 0.0f;
+            sV[j * (DP + 4) + d] = ok ? to_f32(v[base + (size_t)(n0 + j) * D + d]) : 0.0f;
         }
         __syncthreads();
-        float s[FA_BC / 4];
-        float tile_max = -INFINITY;
+        float sc[4][4] = {};
+#pragma unroll 4
+        for (int d = 0; d < DP; ++d) {
+            const float4 qa = *reinterpret_cast<const float4*>(sQt + d * LDT + 4 * ty);
+            const float4 kb = *reinterpret_cast<const float4*>(sKt + d * LDT + 4 * tx);
+            const float qv[4] = {qa.x, qa.y, qa.z, qa.w};
+            const float kv[4] = {kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
-        for (int i = 0; i < FA_BC / 4; ++i) {
-            const int j = t + 4 * i;
-            float dot = 0.0f;
-            for (int d = 0; d < D; ++d) dot = fmaf(sq[r * dpad + d], sk[j * dpad + d], dot);
-            const int key = n0 + j;
-            const bool valid = key < S && !(causal && key > row);
-            s[i] = valid ? dot * scale_log2 : -INFINITY;
-            tile_max = fmaxf(tile_max, s[i]);
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) sc[a][b] = fmaf(qv[a], kv[b], sc[a][b]);
         }
-        tile_max = fmaxf(tile_max, __shfl_xor_sync(0xffffffffu, tile_max, 1));
-        tile_max = fmaxf(tile_max, __shfl_xor_sync(0xffffffffu, tile_max, 2));
-        const float m_new = fmaxf(m_run, tile_max);
-        // Rows with nothing valid yet keep m_new = -inf; use 0 as the shift so exp2 stays finite.
-        const float m_use = m_new == -INFINITY ? 0.0f : m_new;
-        const float alpha = exp2f(m_run - m_use);
-        float psum = 0.0f;
+        float alpha[4];
 #pragma unroll
-        for (int i = 0; i < FA_BC / 4; ++i) {
-            const float p = exp2f(s[i] - m_use);
-            psum += p;
-            sp[r * (FA_BC + 1) + t + 4 * i] = p;
+        for (int a = 0; a < 4; ++a) {
+            const int row = m0 + 4 * ty + a;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int key = n0 + 4 * tx + b;
+                const bool valid = key < S && !(causal && key > row);
+                sc[a][b] = valid ? sc[a][b] * scale_log2 : -INFINITY;
+                mx = fmaxf(mx, sc[a][b]);
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float m_new = fmaxf(m_run[a], mx);
+            // Rows with nothing visible yet keep m_new = -inf; shift by 0 so exp2 stays finite.
+            const float m_use = m_new == -INFINITY ? 0.0f : m_new;
+            alpha[a] = exp2f(m_run[a] - m_use);
+            float psum = 0.0f;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const float p = exp2f(sc[a][b] - m_use);
+                psum += p;
+                sP[(4 * ty + a) * (FA_BC + 4) + 4 * tx + b] = p;
+            }
+#pragma unroll
+            for (int off = 1; off < 16; off <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
+            l_run[a] = l_run[a] * alpha[a] + psum;
+            m_run[a] = m_new;
         }
-        psum += __shfl_xor_sync(0xffffffffu, psum, 1);
-        psum += __shfl_xor_sync(0xffffffffu, psum, 2);
-        l_run = l_run * alpha + psum;
-        m_run = m_new;
-        __syncwarp();
+        __syncthreads();
 #pragma unroll
-        for (int i = 0; i < FA_MAX_D / 4; ++i) {
-            const int d = t + 4 * i;
-            if (d < D) {
-                float acc = 0.0f;
-                for (int j = 0; j < FA_BC; ++j) acc = fmaf(sp[r * (FA_BC + 1) + j], sv[j * D + d], acc);
-                o[i] = o[i] * alpha + acc;
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+            for (int c = 0; c < DT; ++c) o[a][c] *= alpha[a];
+#pragma unroll 4
+        for (int j = 0; j < FA_BC; ++j) {
+            float pv[4];
+#pragma unroll
+            for (int a = 0; a < 4; ++a) pv[a] = sP[(4 * ty + a) * (FA_BC + 4) + j];
+#pragma unroll
+            for (int c = 0; c < DT; ++c) {
+                const float vv = sV[j * (DP + 4) + tx + 16 * c];
+#pragma unroll
+                for (int a = 0; a < 4; ++a) o[a][c] = fmaf(pv[a], vv, o[a][c]);
             }
         }
     }
-    if (row < S) {
-        const float inv = 1.0f / l_run;
 #pragma unroll
-        for (int i = 0; i < FA_MAX_D / 4; ++i) {
-            const int d = t + 4 * i;
-            if (d < D) store_out(out + base + (size_t)row * D + d, o[i] * inv);
+    for (int a = 0; a < 4; ++a) {
+        const int row = m0 + 4 * ty + a;
+        if (row >= S) continue;
+        const float inv = 1.0f / l_run[a];
+#pragma unroll
+        for (int c = 0; c < DT; ++c) {
+            const int d = tx + 16 * c;
+            if (d < D) store_out(out + base + (size_t)row * D + d, o[a][c] * inv);
         }
     }
 }
@@ -296,25 +325,33 @@ template cudaError_t conv2d_simt_launch<float>(float*, const float*, const float
 template cudaError_t conv2d_simt_launch<__nv_bfloat16>(float*, const __nv_bfloat16*, const __nv_bfloat16*, const float*,
                                                        const Conv2dShape&, cudaStream_t);
 
-template <typename T, int BR>
-static cudaError_t flash_attn_simt_launch_br(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
+template <typename T, int DT>
+static cudaError_t flash_attn_simt_launch_dt(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
                                              cudaStream_t stream) {
-    const size_t smem = sizeof(float) * ((size_t)BR * (D + 1) + (size_t)FA_BC * (D + 1) + (size_t)FA_BC * D + BR * (FA_BC + 1));
-    cudaError_t e = cudaFuncSetAttribute(flash_attn_simt_kernel<T, BR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    constexpr int DP = 16 * DT;
+    const size_t smem = sizeof(float) * ((size_t)2 * DP * (FA_BR + 4) + (size_t)FA_BC * (DP + 4) + (size_t)FA_BR * (FA_BC + 4));
+    cudaError_t e = cudaFuncSetAttribute(flash_attn_simt_kernel<T, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((S + BR - 1) / BR, B * H);
+    dim3 grid((S + FA_BR - 1) / FA_BR, B * H);
     const float scale_log2 = scale * 1.4426950408889634f;  // scores in the exp2 domain
-    flash_attn_simt_kernel<T, BR><<<grid, BR * 4, smem, stream>>>(out, q, k, v, H, S, D, scale_log2, causal);
+    flash_attn_simt_kernel<T, DT><<<grid, 256, smem, stream>>>(out, q, k, v, H, S, D, scale_log2, causal);
     return cudaGetLastError();
 }
 
 template <typename T>
 cudaError_t flash_attn_simt_launch(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
                                    cudaStream_t stream) {
-    if (D > FA_MAX_D) {
-        return cudaErrorInvalidValue;
+    switch ((D + 15) / 16) {
+        case 1: return flash_attn_simt_launch_dt<T, 1>(out, q, k, v, B, H, S, D, scale, causal, stream);
+        case 2: return flash_attn_simt_launch_dt<T, 2>(out, q, k, v, B, H, S, D, scale, causal, stream);
+        case 3: return flash_attn_simt_launch_dt<T, 3>(out, q, k, v, B, H, S, D, scale, causal, stream);
+        case 4: return flash_attn_simt_launch_dt<T, 4>(out, q, k, v, B, H, S, D, scale, causal, stream);
+        case 5: return flash_attn_simt_launch_dt<T, 5>(out, q, k, v, B, H, S, D, scale, causal, stream);
+        case 6: return flash_attn_simt_launch_dt<T, 6>(out, q, k, v, B, H, S, D, scale, causal, stream);
+        case 7: return flash_attn_simt_launch_dt<T, 7>(out, q, k, v, B, H, S, D, scale, causal, stream);
+        case 8: return flash_attn_simt_launch_dt<T, 8>(out, q, k, v, B, H, S, D, scale, causal, stream);
+        default: return cudaErrorInvalidValue;
     }
-    return flash_attn_simt_launch_br<T, 64>(out, q, k, v, B, H, S, D, scale, causal, stream);
 }
 template cudaError_t flash_attn_simt_launch<float>(float*, const float*, const float*, const float*, int, int, int, int, float, int,
                                                    cudaStream_t);

@@ -205,6 +205,40 @@ def test_bf16_flash_attention_vs_oracle(cuda_device, S, D, causal):
     np.testing.assert_allclose(out.float().cpu().numpy(), expect, **BF16_TOL)
 
 
+def test_bf16_flash_attention_odd_head_count(cuda_device):
+    """15 (b,h) pairs: the tensor-core kernel's head groups are 8 wide, so the last group holds 7
+    heads; every head and query row must still be computed exactly once."""
+    torch = _torch()
+    rng = np.random.default_rng(15)
+    shape = (3, 5, 1000, 128)
+    q, k, v = (workloads.bf16_bits(rng.standard_normal(shape, dtype=np.float32)) for _ in range(3))
+    scale = 1.0 / math.sqrt(128)
+    expect = oracle.flash_attention(q, k, v, tiles=(128, 128), scale=scale, causal=True)
+    out = torch.full(shape, float("nan"), dtype=torch.bfloat16, device=cuda_device)
+    kernels.flash_attention(out, _to_torch(q, cuda_device), _to_torch(k, cuda_device), _to_torch(v, cuda_device), scale, True)
+    torch.cuda.synchronize()
+    assert runtime.last_kernel() == "flash_fwd_tc_kernel"
+    assert runtime.device_status() == 0
+    np.testing.assert_allclose(out.float().cpu().numpy(), expect, **BF16_TOL)
+
+
+@pytest.mark.parametrize("S,D,causal", [(200, 16, False), (130, 40, True), (257, 64, True), (96, 100, False), (333, 128, True)])
+def test_f32_flash_attention_cuda_cores_vs_oracle(cuda_device, S, D, causal):
+    """fp32 attention on the CUDA-core kernel, one head-dim width per case (16 columns per thread
+    group), sequence tails inside a 64-row block, within the fp32 tolerance."""
+    torch = _torch()
+    rng = np.random.default_rng(1000 + S + D)
+    shape = (1, 3, S, D)
+    q, k, v = (rng.standard_normal(shape, dtype=np.float32) for _ in range(3))
+    scale = 1.0 / math.sqrt(D)
+    expect = oracle.flash_attention(q, k, v, tiles=(64, 64), scale=scale, causal=causal)
+    out = torch.full(shape, float("nan"), device=cuda_device)
+    kernels.flash_attention(out, _to_torch(q, cuda_device), _to_torch(k, cuda_device), _to_torch(v, cuda_device), scale, causal)
+    torch.cuda.synchronize()
+    assert runtime.last_kernel() == "flash_attn_simt_kernel<f32>"
+    np.testing.assert_allclose(out.cpu().numpy(), expect, **FP32_TOL)
+
+
 def test_c5_full_size_sampled_rows(cuda_device):
     """C5: causal bf16 4x32x8192x128. Sampled (b,h) pairs and query rows vs the oracle (first
     rows, a tile boundary, the last rows: the causal diagonal); every row's output is a convex
@@ -278,6 +312,8 @@ def test_typed_entries_report_errors_without_launching(cuda_device):
     ((1, 3, 20, 30), 8, (5, 5), (1, 1), (2, 1), (2, 1, 0, 3), True),          # C % 8 != 0, dilation, asymmetric pads
     ((2, 72, 9, 200), 40, (3, 1), (1, 1), (1, 1), (0, 0, 0, 0), False),        # WO > 128: several tiles per row
     ((1, 8, 10, 12), 200, (1, 1), (1, 1), (1, 1), (0, 0, 0, 0), True),         # F > 128: several column tiles
+    ((3, 136, 17, 72), 300, (3, 3), (1, 1), (1, 1), (1, 1, 1, 1), True),      # channel block tail, F > 256, 2 pixel chunks
+    ((1, 24, 7, 64), 64, (2, 2), (1, 1), (3, 2), (2, 0, 1, 1), False),        # dilation beyond the kernel, F = 64 tiles
 ])
 def test_bf16_conv2d_tensor_cores_vs_oracle(cuda_device, x_shape, f, k, stride, dilation, pads, with_bias):
     torch = _torch()
