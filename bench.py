@@ -38,7 +38,8 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="C4", choices=["C1", "C2", "C3", "C4", "C5"])
+    ap.add_argument("--config", default="C4", choices=["C1", "C2", "C3", "C4", "C5", "X1"],
+                    help="C1-C5: the BASELINE configurations; X1: the bf16 tensor-core conv2d extension workload")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-suite", action="store_true", help="skip the other configurations")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -215,14 +216,17 @@ class Workload:
             full = 4 * s["S"] * s["S"] * s["D"] * (b1 - b0)
             self.flops = full // 2 if s["causal"] else full
             self.kernel_name = None
-        else:  # conv2d: batch 1, one replica per rank
-            self.x = to_device(inp["input"], dev)
+        else:  # conv2d: sharded by batch (C2 has batch 1: one replica per rank)
+            b0, b1 = shard_range(s["B"], rank, world) if s["B"] >= world else (0, s["B"])
+            self.rows = (b0, b1)
+            self.x_host = np.ascontiguousarray(inp["input"][b0:b1])
+            self.x = to_device(self.x_host, dev)
             self.w = to_device(inp["weight"], dev)
             HO = (s["XH"] + s["pads"][0] + s["pads"][1] - s["dilation"][0] * (s["KH"] - 1) - 1) // s["stride"][0] + 1
             WO = (s["XW"] + s["pads"][2] + s["pads"][3] - s["dilation"][1] * (s["KW"] - 1) - 1) // s["stride"][1] + 1
-            self.out = torch.empty(s["B"], s["F"], HO, WO, device=dev)
-            self.flops = cfg.flops
-            self.kernel_name = "conv2d_simt_kernel<f32>"
+            self.out = torch.empty(b1 - b0, s["F"], HO, WO, device=dev)
+            self.flops = cfg.flops * (b1 - b0) // s["B"]
+            self.kernel_name = None
 
     def step(self, stream):
         c, s = self.cfg, self.cfg.shape
@@ -290,7 +294,7 @@ def e2e_run(cfg, wl, steps, world):
         out = torch.empty(shape, dtype=args[0].dtype).pin_memory()
         call = lambda: kernels.flash_attention_inputs_dynamic_tile_dynamic_kernel(out, *args, *cfg.tiles, s["scale"], s["causal"])  # noqa: E731
     else:
-        args = [_pinned(wl.host["input"]), _pinned(wl.host["weight"])]
+        args = [_pinned(wl.x_host), _pinned(wl.host["weight"])]
         out = torch.empty(tuple(wl.out.shape), dtype=torch.float32).pin_memory()
         call = lambda: kernels.conv2d_inputs_dynamic_tile_dynamic_kernel(  # noqa: E731
             out, args[0], args[1], None, *s["stride"], *s["dilation"], *s["pads"], *cfg.tiles)
@@ -351,12 +355,13 @@ def cpu_sample(cfg, threads, budget_rows=None):
             flops = cfg.flops
             desc = "full workload"
     else:
+        nb = 1 if s["B"] > 1 else s["B"]  # batched conv: the first image
         t0 = time.perf_counter()
-        oracle.conv2d(inp["input"], inp["weight"], None, stride=s["stride"], dilation=s["dilation"], pads=s["pads"], tiles=cfg.tiles,
-                      impl=impl, threads=t_threads)
+        oracle.conv2d(np.ascontiguousarray(inp["input"][:nb]), inp["weight"], None, stride=s["stride"], dilation=s["dilation"],
+                      pads=s["pads"], tiles=cfg.tiles, impl=impl, threads=t_threads)
         dt = time.perf_counter() - t0
-        flops = cfg.flops
-        desc = "full workload"
+        flops = cfg.flops * nb // s["B"]
+        desc = "full workload" if nb == s["B"] else f"image 0 of {s['B']}, {flops / 1e9:.1f} GFLOP"
     return flops / dt / 1e12, dt, kind, desc, t_threads
 
 
@@ -367,7 +372,7 @@ def reference_arm(args):
         return 0
     from kernelcode_generate_b200 import workloads
 
-    cfg = workloads.CONFIGS[args.config]
+    cfg = workloads.ALL_CONFIGS[args.config]
     threads = os.cpu_count() or 1
     for _ in range(args.warmup if cfg.kernel != "matmul" or cfg.dtype != "bf16" else 0):
         cpu_sample(cfg, threads)
@@ -392,9 +397,17 @@ def reference_arm(args):
     return 0
 
 
+def launches_per_step(kernel: str) -> int:
+    """Kernels of this library one step launches: the tensor-core conv2d repacks its input and
+    weights (two kernels) before the GEMM kernel; every other path is one kernel."""
+    return 3 if kernel == "conv2d_tc_kernel" else 1
+
+
 def workload_config(cfg, n_gpus):
-    sharding = {"matmul": "contiguous row blocks of M", "flash_attention": "batch x heads",
-                "conv2d": "replicas (batch 1)"}[cfg.kernel]
+    if cfg.kernel == "conv2d":
+        sharding = "batch" if cfg.shape["B"] >= n_gpus else "replicas (batch 1)"
+    else:
+        sharding = {"matmul": "contiguous row blocks of M", "flash_attention": "batch x heads"}[cfg.kernel]
     return {"workload": f"{cfg.name}: {cfg.note}", **{k: v for k, v in cfg.shape.items()}, "sharding": sharding,
             "parallelism": f"shard{n_gpus}", "l2": "256 MiB L2 flush between timed steps (outside the events)"}
 
@@ -412,7 +425,7 @@ def main(argv=None):
     dev = torch.device("cuda", local)
     peaks, peak_src = load_peaks()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-    cfg = workloads.CONFIGS[args.config]
+    cfg = workloads.ALL_CONFIGS[args.config]
     wl = Workload(cfg, rank, world, dev)
     with ClockSampler(local) as clocks:
         job_ms, launch_ms, kernel = time_steps(wl, args.steps, args.warmup, world, flush)
@@ -428,16 +441,17 @@ def main(argv=None):
 
     suite = {}
     if not args.no_suite:
-        for name in ("C1", "C2", "C3", "C5"):
+        for name in ("C1", "C2", "C3", "C5", "X1"):
             if name == cfg.name:
                 continue
-            c = workloads.CONFIGS[name]
+            c = workloads.ALL_CONFIGS[name]
             w2 = Workload(c, rank, world, dev)
             steps = max(3, min(args.steps, 10))
             ms, per_launch, k2 = time_steps(w2, steps, max(3, args.warmup), world, flush)
             tot = reduce_sum(float(w2.flops), world)
             v2 = tot * steps / (ms * 1e-3) / 1e12
             suite[name] = {"value": round(v2, 3), "unit": "TFLOP/s", "ms_per_step": round(ms / steps, 4), "kernel": k2,
+                           "launches_per_step": launches_per_step(k2),
                            "frac_of_bf16_peak": round(v2 / (tensor_peak * world), 4), "workload": c.note}
             del w2
             torch.cuda.empty_cache()
@@ -462,7 +476,7 @@ def main(argv=None):
                          "algorithmic_flop_per_launch": int(wl.flops)},
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * launches_per_step(kernel),
             "clocks": clocks.summary(),
             "suite": suite,
         }

@@ -216,6 +216,36 @@ int matmul_impl(float* out, const void* lhs, const void* rhs, int in_dtype, cons
     return fail(KG_ERR_UNSUPPORTED, "matmul: input dtype code %d not supported (f32=1, bf16=5)", in_dtype);
 }
 
+kg::ConvTcShape conv_tc_shape(const kg::Conv2dShape& s) {
+    kg::ConvTcShape t{s.B, s.C, (s.C + 7) / 8 * 8, s.XH, s.XW, s.F, s.KH, s.KW, s.HO, s.WO, s.sh, s.sw, s.dh, s.dw,
+                      s.pt, s.pb, s.pl, s.pr};
+    // When WO is a multiple of 4, widen the right border of the padded copy (zero columns no output
+    // pixel reads) so the padded row pitch is one too: the epilogue then stores 4-pixel float4 groups.
+    const int xwp = s.XW + s.pl + s.pr;
+    if (s.WO % 4 == 0) t.pr += (4 - xwp % 4) % 4;
+    return t;
+}
+
+// Repack into `scratch` (conv2d_tc_scratch_bytes(t) bytes), build the two tensor maps, launch.
+int conv2d_tc_run(float* out, const void* input, const void* weight, const float* bias, const kg::ConvTcShape& t, void* scratch,
+                  const DeviceInfo* dev, cudaStream_t stream) {
+    KG_CUDA_TRY(kg::conv2d_tc_repack(scratch, static_cast<const __nv_bfloat16*>(input), static_cast<const __nv_bfloat16*>(weight), t,
+                                     stream));
+    const void* w_ftc = static_cast<const char*>(scratch) + kg::conv2d_tc_weight_offset(t);
+    CUtensorMap tx, tw;
+    const cuuint64_t xd[2] = {(cuuint64_t)t.Cp, (cuuint64_t)kg::conv_tc_rows(t)};
+    const cuuint64_t xs[1] = {(cuuint64_t)t.Cp * 2};
+    const cuuint32_t xb[2] = {64, 128};
+    const cuuint64_t wd[3] = {(cuuint64_t)t.Cp, (cuuint64_t)(t.KH * t.KW), (cuuint64_t)t.F};
+    const cuuint64_t ws[2] = {(cuuint64_t)t.Cp * 2, (cuuint64_t)t.KH * t.KW * t.Cp * 2};
+    const cuuint32_t wb[3] = {64, 1, (cuuint32_t)(kg::conv2d_tc_block_n(t.F) / 2)};
+    int rc;
+    if ((rc = make_tmap_bf16(&tx, scratch, 2, xd, xs, xb)) || (rc = make_tmap_bf16(&tw, w_ftc, 3, wd, ws, wb))) return rc;
+    g_last_kernel = "conv2d_tc_kernel";
+    KG_CUDA_TRY(kg::conv2d_tc_launch(tx, tw, out, bias, t, dev->num_sms, dev->status, stream));
+    return KG_OK;
+}
+
 int conv2d_impl(float* out, const void* input, const void* weight, int in_dtype, const float* bias, const kg::Conv2dShape& s,
                 cudaStream_t stream) {
     if (!out || !input || !weight) return fail(KG_ERR_INVALID_ARGUMENT, "conv2d: null pointer");
@@ -225,34 +255,14 @@ int conv2d_impl(float* out, const void* input, const void* weight, int in_dtype,
         return KG_OK;
     }
     if (in_dtype == KG_DTYPE_BF16) {
-        kg::ConvTcShape t{s.B, s.C, (s.C + 7) / 8 * 8, s.XH, s.XW, s.F, s.KH, s.KW, s.HO, s.WO, s.sh, s.sw, s.dh, s.dw,
-                          s.pt, s.pb, s.pl, s.pr, 0, 0};
-        t.tile_w = t.WO < 128 ? t.WO : 128;
-        t.rows = 128 / t.tile_w < t.HO ? 128 / t.tile_w : t.HO;
-        if (kg::conv2d_tc_supported(t) && aligned16(out)) {
+        const kg::ConvTcShape t = conv_tc_shape(s);
+        if (kg::conv2d_tc_supported(t)) {
             DeviceInfo* dev = nullptr;
             int rc = device_info(&dev);
             if (rc != KG_OK) return rc;
-            const size_t x_elems = static_cast<size_t>(t.B) * t.XH * t.XW * t.Cp;
-            const size_t w_elems = static_cast<size_t>(t.F) * t.KH * t.KW * t.Cp;
-            const size_t x_bytes = (x_elems * 2 + 255) & ~size_t(255);
             void* scratch = nullptr;
-            if ((rc = device_scratch(x_bytes + w_elems * 2, &scratch))) return rc;
-            __nv_bfloat16* x_nhwc = static_cast<__nv_bfloat16*>(scratch);
-            __nv_bfloat16* w_ftc = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(scratch) + x_bytes);
-            KG_CUDA_TRY(kg::conv2d_tc_repack(x_nhwc, w_ftc, static_cast<const __nv_bfloat16*>(input),
-                                             static_cast<const __nv_bfloat16*>(weight), t, stream));
-            CUtensorMap tx, tw;
-            const cuuint64_t xd[4] = {(cuuint64_t)t.Cp, (cuuint64_t)t.XW, (cuuint64_t)t.XH, (cuuint64_t)t.B};
-            const cuuint64_t xs[3] = {(cuuint64_t)t.Cp * 2, (cuuint64_t)t.XW * t.Cp * 2, (cuuint64_t)t.XH * t.XW * t.Cp * 2};
-            const cuuint32_t xb[4] = {64, (cuuint32_t)t.tile_w, (cuuint32_t)t.rows, 1};
-            const cuuint64_t wd[3] = {(cuuint64_t)t.Cp, (cuuint64_t)(t.KH * t.KW), (cuuint64_t)t.F};
-            const cuuint64_t ws[2] = {(cuuint64_t)t.Cp * 2, (cuuint64_t)t.KH * t.KW * t.Cp * 2};
-            const cuuint32_t wb[3] = {64, 1, (cuuint32_t)kg::conv2d_tc_block_n(t.F)};
-            if ((rc = make_tmap_bf16(&tx, x_nhwc, 4, xd, xs, xb)) || (rc = make_tmap_bf16(&tw, w_ftc, 3, wd, ws, wb))) return rc;
-            g_last_kernel = "conv2d_tc_kernel";
-            KG_CUDA_TRY(kg::conv2d_tc_launch(tx, tw, out, bias, t, dev->status, stream));
-            return KG_OK;
+            if ((rc = device_scratch(kg::conv2d_tc_scratch_bytes(t), &scratch))) return rc;
+            return conv2d_tc_run(out, input, weight, bias, t, scratch, dev, stream);
         }
         g_last_kernel = "conv2d_simt_kernel<bf16>";
         KG_CUDA_TRY(kg::conv2d_simt_launch(out, static_cast<const __nv_bfloat16*>(input), static_cast<const __nv_bfloat16*>(weight),
@@ -626,14 +636,9 @@ extern "C" int kg_sm100_conv2d_noalloc(float* out, const void* input, const void
     int rc = conv2d_shape(&s, B, C, XH, XW, F, KH, KW, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_bottom, pad_left,
                           pad_right);
     if (rc != KG_OK) return rc;
-    kg::ConvTcShape t{s.B, s.C, (s.C + 7) / 8 * 8, s.XH, s.XW, s.F, s.KH, s.KW, s.HO, s.WO, s.sh, s.sw, s.dh, s.dw,
-                      s.pt, s.pb, s.pl, s.pr, 0, 0};
-    t.tile_w = t.WO < 128 ? t.WO : 128;
-    t.rows = 128 / t.tile_w < t.HO ? 128 / t.tile_w : t.HO;
-    if (!kg::conv2d_tc_supported(t) || !aligned16(out))
-        return fail(KG_ERR_UNSUPPORTED, "conv2d_noalloc: only the tensor-core path (stride 1, 16-byte aligned out)");
-    const size_t x_bytes = (static_cast<size_t>(t.B) * t.XH * t.XW * t.Cp * 2 + 255) & ~size_t(255);
-    const size_t need = x_bytes + static_cast<size_t>(t.F) * t.KH * t.KW * t.Cp * 2;
+    const kg::ConvTcShape t = conv_tc_shape(s);
+    if (!kg::conv2d_tc_supported(t)) return fail(KG_ERR_UNSUPPORTED, "conv2d_noalloc: only the tensor-core path (stride 1)");
+    const size_t need = kg::conv2d_tc_scratch_bytes(t);
     if (need > KG_CONV2D_NOALLOC_SCRATCH_BYTES)
         return fail(KG_ERR_UNSUPPORTED, "conv2d_noalloc: needs %zu bytes of scratch, the fixed array holds %zu", need,
                     static_cast<size_t>(KG_CONV2D_NOALLOC_SCRATCH_BYTES));
@@ -641,22 +646,7 @@ extern "C" int kg_sm100_conv2d_noalloc(float* out, const void* input, const void
     if ((rc = device_info(&dev))) return rc;
     void* scratch = nullptr;
     if ((rc = noalloc_scratch(&scratch))) return rc;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    __nv_bfloat16* x_nhwc = static_cast<__nv_bfloat16*>(scratch);
-    __nv_bfloat16* w_ftc = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(scratch) + x_bytes);
-    // The repack writes every element the conv kernel reads (channel padding included), so the
-    // previous call's contents need no clearing.
-    KG_CUDA_TRY(kg::conv2d_tc_repack(x_nhwc, w_ftc, static_cast<const __nv_bfloat16*>(input), static_cast<const __nv_bfloat16*>(weight), t,
-                                     st));
-    CUtensorMap tx, tw;
-    const cuuint64_t xd[4] = {(cuuint64_t)t.Cp, (cuuint64_t)t.XW, (cuuint64_t)t.XH, (cuuint64_t)t.B};
-    const cuuint64_t xs[3] = {(cuuint64_t)t.Cp * 2, (cuuint64_t)t.XW * t.Cp * 2, (cuuint64_t)t.XH * t.XW * t.Cp * 2};
-    const cuuint32_t xb[4] = {64, (cuuint32_t)t.tile_w, (cuuint32_t)t.rows, 1};
-    const cuuint64_t wd[3] = {(cuuint64_t)t.Cp, (cuuint64_t)(t.KH * t.KW), (cuuint64_t)t.F};
-    const cuuint64_t ws[2] = {(cuuint64_t)t.Cp * 2, (cuuint64_t)t.KH * t.KW * t.Cp * 2};
-    const cuuint32_t wb[3] = {64, 1, (cuuint32_t)kg::conv2d_tc_block_n(t.F)};
-    if ((rc = make_tmap_bf16(&tx, x_nhwc, 4, xd, xs, xb)) || (rc = make_tmap_bf16(&tw, w_ftc, 3, wd, ws, wb))) return rc;
-    g_last_kernel = "conv2d_tc_kernel";
-    KG_CUDA_TRY(kg::conv2d_tc_launch(tx, tw, out, bias, t, dev->status, st));
-    return KG_OK;
+    // The repack writes every element the conv kernel reads (border and channel padding included),
+    // so the previous call's contents need no clearing.
+    return conv2d_tc_run(out, input, weight, bias, t, scratch, dev, static_cast<cudaStream_t>(stream));
 }

@@ -1,270 +1,452 @@
-// bf16 conv2d as an implicit GEMM on tcgen05 tensor cores, over NHWC tiles.
+// bf16 conv2d as an implicit GEMM on tcgen05 tensor cores (CTA pairs), over a padded NHWC copy.
 //
 // Computes the reference conv2d loop nest (kernel/conv2d/inputs_dynamic_tile_dynamic.py:142-205:
 // out[b,f,ho,wo] = sum_{c,kh,kw} weight[f,c,kh,kw] * input[b,c,ho*sh-pt+kh*dh, wo*sw-pl+kw*dw],
 // zero outside the input) for bf16 inputs with f32 accumulation and f32 NCHW output, stride 1.
 //
-//   1. Repack (scratch): input NCHW -> NHWC with channels padded to a multiple of 8 (TMA row
-//      stride), weights OIHW -> [F, KH*KW, C] likewise.
-//   2. GEMM rows = output pixels (TMEM lanes), columns = output channels, reduction =
-//      (kh, kw, 64-channel block). The A tile of one reduction step is ONE 4-D TMA box of the NHWC
-//      input {64 channels, tile_w pixels, R rows, 1 image} at (c0, wo0 - pl + kw*dw,
-//      ho0 - pt + kh*dh, b): the im2col gather is the TMA's addressing, and out-of-range
-//      coordinates (the padding) read zeros. R = 128 / tile_w output rows share one tile when the
-//      output row is shorter than 128 pixels.
-//   3. Epilogue: lane = pixel, so each f column is a coalesced run of output pixels in NCHW.
-// warp 0 TMA producer (4-stage ring), warp 1 MMA issuer (one accumulator, one tile per CTA),
-// warps 2-5 epilogue.
+//   1. Repack (scratch): input NCHW -> x_pad [B, XHp, XWp, Cp] with the padding written as zero
+//      rows/columns (XHp = XH+pt+pb, XWp = XW+pl+pr) and channels padded to a multiple of 8;
+//      weights OIHW -> [F, KH*KW, Cp].
+//   2. GEMM rows = padded pixels p = (b*XHp + ho)*XWp + wo, columns = filters, reduction =
+//      (tap, 64-channel block). Output pixel (b, ho, wo) reads x_pad[b, ho+kh*dh, wo+kw*dw], which is
+//      row p + kh*dh*XWp + kw*dw of x_pad viewed as a [B*XHp*XWp, Cp] matrix: every tap's A tile is
+//      one 2-D TMA box of 128 consecutive rows, shifted. Rows with wo >= WO or ho >= HO are
+//      computed and dropped (for 56x56 outputs with pad 1: 3136 of 3364 rows kept, 93 %).
+//   3. Epilogue: TMEM lane = pixel, so each filter column is a coalesced run of output pixels.
+//
+// Kernel structure as the pair GEMM (kg_gemm_tc2.cu): a cluster of 2 CTAs owns a 256-pixel x PBN-filter
+// tile; each CTA loads its own 128 pixel rows of A and PBN/2 filter rows of B (no multicast), the
+// even CTA issues tcgen05.mma.cta_group::2 256xPBNx16; the accumulator is double-buffered in TMEM so
+// the epilogue of one tile overlaps the MMAs of the next; pairs walk the tiles persistently.
 #include "kg_conv_tc.h"
 #include "kg_ptx.cuh"
 
 namespace kg {
 namespace {
 
-constexpr int BM = 128;
+constexpr int PBM = 256;  // pixels per pair tile (128 per CTA)
 constexpr int BK = 64;
-constexpr int STAGES = 4;
+constexpr int GROUP_M = 8;
 constexpr int NUM_THREADS = 192;
-constexpr uint32_t A_STAGE_BYTES = BM * BK * 2;  // 16 KiB
+constexpr uint32_t A_STAGE_BYTES = 128 * BK * 2;  // 16 KiB
+constexpr uint16_t PAIR_MASK = 0x3;
 
-struct alignas(8) ConvBars {
+template <int PBN>
+struct ConvPairCfg {
+    static constexpr int BNC = PBN / 2;                           // filters loaded by each CTA
+    static constexpr int STAGES = PBN == 256 ? 6 : 8;
+    static constexpr uint32_t B_STAGE_BYTES = BNC * BK * 2;
+    static constexpr uint32_t TMEM_COLS = 2 * PBN;                // two accumulators
+    static constexpr uint32_t IDESC = idesc_f16(PBM, PBN, true, true, false, false);
+};
+
+constexpr int EPI_THREADS = 128;
+constexpr uint32_t OUT_CHUNK_BYTES = 32 * 128 * 4;  // 32 filters x 128 pixels of f32
+
+template <int STAGES>
+struct alignas(8) ConvPairBars {
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
-    uint64_t acc_full;
+    uint64_t tfull[2];
+    uint64_t tempty[2];
+    uint64_t drain;
+    uint64_t epi;  // the 128 epilogue threads, once per 32-filter chunk
     uint32_t tmem_base;
     int abort;
 };
 
-template <int BN>
-struct ConvCfg {
-    static constexpr uint32_t B_STAGE_BYTES = BN * BK * 2;
-    static constexpr uint32_t TMEM_COLS = BN < 32 ? 32 : BN;
-    static constexpr uint32_t IDESC = idesc_f16(BM, BN, true, true, false, false);
-    static constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + sizeof(ConvBars);
-};
+template <int PBN>
+constexpr size_t conv_smem_bytes() {
+    using Cfg = ConvPairCfg<PBN>;
+    return 1024 + Cfg::STAGES * (A_STAGE_BYTES + Cfg::B_STAGE_BYTES) + 2 * OUT_CHUNK_BYTES + sizeof(ConvPairBars<Cfg::STAGES>);
+}
 
-template <int BN>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__device__ __forceinline__ void conv_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+    const int per_group = GROUP_M * num_n;
+    const int group = tile / per_group;
+    const int first_m = group * GROUP_M;
+    const int gsize = min(num_m - first_m, GROUP_M);
+    const int in_group = tile - group * per_group;
+    mb = first_m + in_group % gsize;
+    nb = in_group / gsize;
+}
+
+template <int PBN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     conv2d_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w, float* __restrict__ out,
-                     const float* __restrict__ bias, ConvTcShape s, int* status) {
-    using Cfg = ConvCfg<BN>;
+                     const float* __restrict__ bias, ConvTcShape s, int vec_ok, int* status) {
+    using Cfg = ConvPairCfg<PBN>;
+    constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-    ConvBars* bars = reinterpret_cast<ConvBars*>(sB + STAGES * Cfg::B_STAGE_BYTES);
+    float* sOut = reinterpret_cast<float*>(sB + STAGES * Cfg::B_STAGE_BYTES);  // [2][32 filters][128 pixels]
+    ConvPairBars<STAGES>* bars = reinterpret_cast<ConvPairBars<STAGES>*>(sB + STAGES * Cfg::B_STAGE_BYTES + 2 * OUT_CHUNK_BYTES);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    // tile -> (b, ho0, wo0) for the rows, f0 for the columns
-    const int f0 = blockIdx.y * BN;
-    int t = blockIdx.x;
-    const int w_tiles = (s.WO + s.tile_w - 1) / s.tile_w;
-    const int h_tiles = (s.HO + s.rows - 1) / s.rows;
-    const int wt = t % w_tiles;
-    t /= w_tiles;
-    const int ht = t % h_tiles;
-    const int b = t / h_tiles;
-    const int wo0 = wt * s.tile_w;
-    const int ho0 = ht * s.rows;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1;
+    const int num_pairs = gridDim.x >> 1;
+    const int xhp = s.XH + s.pt + s.pb;
+    const int xwp = s.XW + s.pl + s.pr;
+    const int img = xhp * xwp;
+    const int rows = s.B * img;  // conv2d_tc_supported keeps this and every shifted row below 2^31
+    const int num_m = (rows + PBM - 1) / PBM;
+    const int num_n = (s.F + PBN - 1) / PBN;
+    const int num_tiles = num_m * num_n;
     const int c_blocks = (s.Cp + BK - 1) / BK;
     const int num_k = s.KH * s.KW * c_blocks;
-    const uint32_t a_bytes = static_cast<uint32_t>(BK * 2 * s.tile_w * s.rows);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&bars->full[i], 1);
             mbar_init(&bars->empty[i], 1);
         }
-        mbar_init(&bars->acc_full, 1);
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&bars->tfull[a], 1);
+            mbar_init(&bars->tempty[a], 8);  // lane 0 of the 4 epilogue warps of both CTAs
+        }
+        mbar_init(&bars->drain, 1);
+        mbar_init(&bars->epi, EPI_THREADS);
+        // A kernel that starts after another reported a pipeline timeout does no work.
         bars->abort = (status != nullptr && *reinterpret_cast<volatile int*>(status) != 0) ? 1 : 0;
         fence_barrier_init();
+        tma_prefetch_desc(&tm_x);
+        tma_prefetch_desc(&tm_w);
     }
     if (warp == 1) {
-        tmem_alloc(&bars->tmem_base, Cfg::TMEM_COLS);
-        tmem_relinquish();
+        tmem_alloc_pair(&bars->tmem_base, Cfg::TMEM_COLS);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
     __syncthreads();
+    cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or completion
     tc_fence_after();
     const uint32_t tmem_base = bars->tmem_base;
     volatile int* abort = &bars->abort;
 
     if (warp == 0) {
-        if (lane == 0 && !*abort) {
-            tma_prefetch_desc(&tm_x);
-            tma_prefetch_desc(&tm_w);
+        // ------------------------------------------------------------ TMA producer (both CTAs)
+        if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            int issued = 0;
-            for (int kidx = 0; kidx < num_k; ++kidx) {
-                const int cb = kidx % c_blocks;
-                const int tap = kidx / c_blocks;
-                const int kh = tap / s.KW, kw = tap % s.KW;
-                if (!mbar_wait(&bars->empty[stage], phase ^ 1u, abort, status, kDevTimeoutProducer)) break;
-                mbar_arrive_expect_tx(&bars->full[stage], a_bytes + Cfg::B_STAGE_BYTES);
-                tma_load_4d(sA + stage * A_STAGE_BYTES, &tm_x, &bars->full[stage], cb * BK, wo0 - s.pl + kw * s.dw,
-                            ho0 - s.pt + kh * s.dh, b);
-                tma_load_3d(sB + stage * Cfg::B_STAGE_BYTES, &tm_w, &bars->full[stage], cb * BK, tap, f0);
-                ++issued;
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1u;
+            uint32_t issued = 0;
+            for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs) {
+                int mb, nb;
+                conv_tile_coords(tile, num_m, num_n, mb, nb);
+                const int row0 = mb * PBM + static_cast<int>(rank) * 128;
+                const int f0 = nb * PBN + static_cast<int>(rank) * Cfg::BNC;
+                for (int kidx = 0; kidx < num_k; ++kidx) {
+                    const int tap = kidx / c_blocks;
+                    const int cb = kidx - tap * c_blocks;
+                    const int kh = tap / s.KW, kw = tap - kh * s.KW;
+                    const int shift = kh * s.dh * xwp + kw * s.dw;
+                    if (!mbar_wait_cluster(&bars->empty[stage], phase ^ 1u, abort, status, kDevTimeoutProducer)) break;
+                    if (leader) mbar_arrive_expect_tx(&bars->full[stage], 2 * (A_STAGE_BYTES + Cfg::B_STAGE_BYTES));
+                    const uint32_t leader_full = mapa_shared(smem_u32(&bars->full[stage]), 0);
+                    tma_load_2d_pair(sA + stage * A_STAGE_BYTES, &tm_x, leader_full, cb * BK, row0 + shift);
+                    tma_load_3d_pair(sB + stage * Cfg::B_STAGE_BYTES, &tm_w, leader_full, cb * BK, tap, f0);
+                    ++issued;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
                 }
             }
-            if (*abort) {
+            if (*abort && leader) {
+                // The even CTA's full barriers count both CTAs' bytes: wait (bounded) for the copies
+                // still in flight before the pair's shared memory goes away.
+                const uint32_t pending = issued < static_cast<uint32_t>(STAGES) ? issued : static_cast<uint32_t>(STAGES);
                 int keep_waiting = 0;
-                const int pending = issued < STAGES ? issued : STAGES;
-                for (int i = 0; i < pending; ++i) {
+                for (uint32_t i = 0; i < pending; ++i) {
                     stage = stage == 0 ? STAGES - 1 : stage - 1;
                     if (stage == STAGES - 1) phase ^= 1u;
-                    mbar_wait(&bars->full[stage], phase, &keep_waiting, nullptr, 0);
+                    mbar_wait_cluster(&bars->full[stage], phase, &keep_waiting, nullptr, 0);
                 }
             }
         }
     } else if (warp == 1) {
-        if (!*abort) {
+        // ------------------------------------------------------------ MMA issuer (even CTA)
+        if (leader) {
             int stage = 0;
             uint32_t phase = 0;
-            bool ok = true;
-            for (int kidx = 0; kidx < num_k; ++kidx) {
-                if (!mbar_wait(&bars->full[stage], phase, abort, status, kDevTimeoutMma)) {
-                    ok = false;
-                    break;
-                }
+            uint32_t acc = 0, acc_phase = 0;
+            for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs) {
+                if (!mbar_wait_cluster(&bars->tempty[acc], acc_phase ^ 1u, abort, status, kDevTimeoutMma)) break;
                 tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
-                    const uint32_t b_base = smem_u32(sB + stage * Cfg::B_STAGE_BYTES);
-#pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk) {
-                        const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
-                        const uint64_t b_desc = smem_desc_sw128(b_base + kk * 32, 16, 1024);
-                        umma_f16(tmem_base, a_desc, b_desc, Cfg::IDESC, (kidx | kk) != 0 ? 1u : 0u);
+                const uint32_t d_tmem = tmem_base + acc * PBN;
+                bool ok = true;
+                for (int kidx = 0; kidx < num_k; ++kidx) {
+                    if (!mbar_wait_cluster(&bars->full[stage], phase, abort, status, kDevTimeoutMma)) {
+                        ok = false;
+                        break;
                     }
-                    umma_commit(&bars->empty[stage]);
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
+                        const uint32_t b_base = smem_u32(sB + stage * Cfg::B_STAGE_BYTES);
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk) {
+                            const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
+                            const uint64_t b_desc = smem_desc_sw128(b_base + kk * 32, 16, 1024);
+                            umma_f16_pair(d_tmem, a_desc, b_desc, Cfg::IDESC, (kidx | kk) != 0 ? 1u : 0u);
+                        }
+                        umma_commit_pair_multicast(&bars->empty[stage], PAIR_MASK);
+                    }
+                    __syncwarp();
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
                 }
+                if (!ok) break;
+                if (lane == 0) umma_commit_pair_multicast(&bars->tfull[acc], PAIR_MASK);
                 __syncwarp();
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1u;
-                }
+                acc ^= 1u;
+                if (acc == 0) acc_phase ^= 1u;
             }
-            if (lane == 0) umma_commit(&bars->acc_full);  // arrives once every MMA issued above is done
+            if (lane == 0) umma_commit_pair(&bars->drain);
             __syncwarp();
-            (void)ok;
-            int keep_waiting = 0;  // drain before the TMEM is released
-            mbar_wait(&bars->acc_full, 0, &keep_waiting, status, kDevTimeoutDrain);
+            int keep_waiting = 0;
+            mbar_wait_cluster(&bars->drain, 0, &keep_waiting, status, kDevTimeoutDrain);
         }
     } else {
-        // epilogue: TMEM lane = output pixel, column = output channel
-        const int quarter = warp & 3;
-        const int r = quarter * 32 + lane;
-        if (!*abort && mbar_wait(&bars->acc_full, 0, abort, status, kDevTimeoutEpilogue)) {
-            tc_fence_after();
-            const int ho = ho0 + r / s.tile_w;
-            const int wo = wo0 + r % s.tile_w;
-            const bool valid = r < s.tile_w * s.rows && ho < s.HO && wo < s.WO;
-            const size_t plane = static_cast<size_t>(s.HO) * s.WO;
-            float* dst = out + (static_cast<size_t>(b) * s.F) * plane + static_cast<size_t>(ho) * s.WO + wo;
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t v[32];
-                tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, v);
-                tmem_wait_ld();
-                if (valid) {
+        // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+        // Per 32-filter chunk: TMEM (lane = pixel) -> shared [filter][pixel] -> each warp stores 8
+        // filter rows, a lane writing 4 consecutive pixels (one float4 when vec_ok: the padded row
+        // pitch and WO are multiples of 4, so an aligned group of 4 pixels is one output run).
+        const int quarter = warp & 3;  // TMEM lane quarter this warp may read
+        const int ew = warp - 2;       // filter rows ew*8 .. ew*8+7 of each chunk in the store phase
+        const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&bars->tempty[0]), 0), mapa_shared(smem_u32(&bars->tempty[1]), 0)};
+        const size_t plane = static_cast<size_t>(s.HO) * s.WO;
+        uint32_t acc = 0, acc_phase = 0, epi_phase = 0;
+        bool alive = true;
+        for (int tile = pair; tile < num_tiles && alive && !*abort; tile += num_pairs) {
+            int mb, nb;
+            conv_tile_coords(tile, num_m, num_n, mb, nb);
+            // this lane's 4 pixels (store phase): padded pixel -> (b, ho, wo); rows outside the output are dropped
+            const int pg = mb * PBM + static_cast<int>(rank) * 128 + 4 * lane;
+            size_t off[4];
+            uint32_t valid = 0;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int f = f0 + c * 32 + j;
-                        if (f < s.F) dst[static_cast<size_t>(f) * plane] = __uint_as_float(v[j]) + (bias != nullptr ? bias[f] : 0.0f);
+            for (int i = 0; i < 4; ++i) {
+                const int p = pg + i;
+                const int b = p / img;
+                const int rem = p - b * img;
+                const int ho = rem / xwp;
+                const int wo = rem - ho * xwp;
+                off[i] = static_cast<size_t>(b) * s.F * plane + static_cast<size_t>(ho) * s.WO + wo;
+                if (p < rows && ho < s.HO && wo < s.WO) valid |= 1u << i;
+            }
+            const bool vec = vec_ok && valid == 0xFu;
+            if (!mbar_wait_cluster(&bars->tfull[acc], acc_phase, abort, status, kDevTimeoutEpilogue)) break;
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * PBN;
+#pragma unroll 1
+            for (int c = 0; c < PBN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(t_row + c * 32, r);
+                tmem_wait_ld();
+                if (c == PBN / 32 - 1) {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+                }
+                float* buf = sOut + (c & 1) * (32 * 128);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) buf[j * 128 + quarter * 32 + lane] = __uint_as_float(r[j]);
+                mbar_arrive(&bars->epi);
+                if (!mbar_wait(&bars->epi, epi_phase, abort, status, kDevTimeoutEpilogue)) {
+                    alive = false;
+                    break;
+                }
+                epi_phase ^= 1u;
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    const int j = ew * 8 + jj;
+                    const int f = nb * PBN + c * 32 + j;
+                    if (f >= s.F) break;
+                    float4 v = *reinterpret_cast<const float4*>(buf + j * 128 + 4 * lane);
+                    if (bias != nullptr) {
+                        const float bf = bias[f];
+                        v.x += bf;
+                        v.y += bf;
+                        v.z += bf;
+                        v.w += bf;
+                    }
+                    const size_t fo = static_cast<size_t>(f) * plane;
+                    if (vec) {
+                        *reinterpret_cast<float4*>(out + off[0] + fo) = v;
+                    } else {
+                        if (valid & 1u) out[off[0] + fo] = v.x;
+                        if (valid & 2u) out[off[1] + fo] = v.y;
+                        if (valid & 4u) out[off[2] + fo] = v.z;
+                        if (valid & 8u) out[off[3] + fo] = v.w;
                     }
                 }
             }
+            acc ^= 1u;
+            if (acc == 0) acc_phase ^= 1u;
         }
     }
 
     tc_fence_before();
     __syncthreads();
+    cluster_sync();  // no CTA leaves while its peer can still arrive on its barriers
     tc_fence_after();
     if (warp == 1) {
-        tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+        tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
     }
 }
 
-// NCHW (C channels) -> NHWC with Cp >= C channels, zero in the padding; 32x32 tiles over (C, H*W).
-__global__ void nchw_to_nhwc_kernel(__nv_bfloat16* __restrict__ dst, const __nv_bfloat16* __restrict__ src, int C, int Cp, int HW) {
-    __shared__ __nv_bfloat16 tile[32][33];
-    const int b = blockIdx.z;
-    const int p0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-    const __nv_bfloat16 zero = __float2bfloat16(0.0f);
-    for (int i = threadIdx.y; i < 32; i += 8) {
-        const int c = c0 + i, p = p0 + threadIdx.x;
-        tile[i][threadIdx.x] = (c < C && p < HW) ? src[(static_cast<size_t>(b) * C + c) * HW + p] : zero;
+// NCHW (C channels) -> padded NHWC [B, XHp, XWp, Cp]: zero border and zero channels C..Cp.
+// Block = one padded row (x = b * XHp + hp) x 64 channels (y); 256 threads. Source pixels go in
+// chunks of 64 through a [pixel][channel] shared tile: each thread loads 8 consecutive pixels of
+// one channel (16 bytes when XW % 8 == 0) and stores 8 consecutive channels of one pixel (16 bytes),
+// so both sides move whole 128-byte lines. Border rows and columns are stored as zeros.
+// The tile's 8-channel groups are XOR-swizzled by the pixel's group of 8 so that the transposing
+// 2-byte stores of one warp land in distinct banks; each group stays 16 contiguous bytes.
+constexpr int RP_PIX = 64, RP_CH = 64;
+__device__ __forceinline__ int rp_col(int px, int c) { return c ^ (((px >> 3) & 7) << 3); }
+
+__global__ void __launch_bounds__(256) nchw_to_padded_nhwc_kernel(__nv_bfloat16* __restrict__ dst, const __nv_bfloat16* __restrict__ src,
+                                                                  ConvTcShape s, int vec_ok) {
+    __shared__ __align__(16) __nv_bfloat16 tile[RP_PIX][RP_CH];
+    const int xhp = s.XH + s.pt + s.pb;
+    const int xwp = s.XW + s.pl + s.pr;
+    const int plane = static_cast<int>(blockIdx.x);
+    const int hp = plane % xhp;
+    const int b = plane / xhp;
+    const int c0 = static_cast<int>(blockIdx.y) * RP_CH;
+    const int nvec = min(RP_CH, s.Cp - c0) / 8;  // 16-byte channel groups this block writes
+    const int h = hp - s.pt;
+    __nv_bfloat16* row = dst + static_cast<size_t>(plane) * xwp * s.Cp + c0;
+    const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
+    if (h < 0 || h >= s.XH) {
+        for (int i = threadIdx.x; i < xwp * nvec; i += 256) {
+            const int px = i / nvec, v = i - px * nvec;
+            *reinterpret_cast<uint4*>(row + static_cast<size_t>(px) * s.Cp + 8 * v) = zero4;
+        }
+        return;
     }
-    __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += 8) {
-        const int p = p0 + i, c = c0 + threadIdx.x;
-        if (p < HW && c < Cp) dst[(static_cast<size_t>(b) * HW + p) * Cp + c] = tile[threadIdx.x][i];
+    for (int i = threadIdx.x; i < (s.pl + s.pr) * nvec; i += 256) {
+        const int k = i / nvec, v = i - k * nvec;
+        const int px = k < s.pl ? k : s.XW + k;  // left border columns, then right ones
+        *reinterpret_cast<uint4*>(row + static_cast<size_t>(px) * s.Cp + 8 * v) = zero4;
+    }
+    const __nv_bfloat16* src_row = src + (static_cast<size_t>(b) * s.C * s.XH + h) * s.XW;  // channel 0 of row h
+    const size_t ch_stride = static_cast<size_t>(s.XH) * s.XW;
+    for (int w0 = 0; w0 < s.XW; w0 += RP_PIX) {
+        for (int i = threadIdx.x; i < RP_CH * (RP_PIX / 8); i += 256) {
+            const int c = i / (RP_PIX / 8), g = i - c * (RP_PIX / 8);
+            const int w = w0 + 8 * g;
+            const int ch = c0 + c;
+            __align__(16) __nv_bfloat16 vals[8];
+            if (ch < s.C && vec_ok && w + 8 <= s.XW) {
+                *reinterpret_cast<uint4*>(vals) = *reinterpret_cast<const uint4*>(src_row + ch * ch_stride + w);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    vals[j] = (ch < s.C && w + j < s.XW) ? src_row[ch * ch_stride + w + j] : __float2bfloat16(0.0f);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) tile[8 * g + j][rp_col(8 * g + j, c)] = vals[j];
+        }
+        __syncthreads();
+        const int npix = min(RP_PIX, s.XW - w0);
+        for (int i = threadIdx.x; i < npix * nvec; i += 256) {
+            const int px = i / nvec, v = i - px * nvec;
+            *reinterpret_cast<uint4*>(row + static_cast<size_t>(s.pl + w0 + px) * s.Cp + 8 * v) =
+                *reinterpret_cast<const uint4*>(&tile[px][rp_col(px, 8 * v)]);
+        }
+        __syncthreads();
     }
 }
 
-// OIHW -> [F, KH*KW, Cp], zero in the channel padding.
+// OIHW -> [F, KH*KW, Cp], zero in the channel padding. One thread per (f, c): it reads the taps of
+// weight[f, c] (contiguous) and writes one element per tap; neighbouring threads write neighbouring c.
 __global__ void weight_to_ftc_kernel(__nv_bfloat16* __restrict__ dst, const __nv_bfloat16* __restrict__ src, int F, int C, int Cp, int taps) {
-    const long long total = static_cast<long long>(F) * taps * Cp;
+    const long long total = static_cast<long long>(F) * Cp;
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int c = static_cast<int>(i % Cp);
-        const int tap = static_cast<int>((i / Cp) % taps);
-        const int f = static_cast<int>(i / (static_cast<long long>(Cp) * taps));
-        dst[i] = c < C ? src[(static_cast<size_t>(f) * C + c) * taps + tap] : __float2bfloat16(0.0f);
+        const int f = static_cast<int>(i / Cp);
+        const int c = static_cast<int>(i - static_cast<long long>(f) * Cp);
+        const __nv_bfloat16* w = src + (static_cast<size_t>(f) * C + c) * taps;
+        __nv_bfloat16* d = dst + static_cast<size_t>(f) * taps * Cp + c;
+        for (int t = 0; t < taps; ++t) d[static_cast<size_t>(t) * Cp] = c < C ? w[t] : __float2bfloat16(0.0f);
     }
 }
 
-template <int BN>
-cudaError_t launch_bn(const CUtensorMap& tm_x, const CUtensorMap& tm_w, float* out, const float* bias, const ConvTcShape& s, int* status,
-                      cudaStream_t stream) {
+template <int PBN>
+cudaError_t launch_pbn(const CUtensorMap& tm_x, const CUtensorMap& tm_w, float* out, const float* bias, const ConvTcShape& s, int num_sms,
+                       int* status, cudaStream_t stream) {
+    constexpr size_t smem = conv_smem_bytes<PBN>();
+    static_assert(smem <= 227 * 1024, "shared memory");
     static bool attr_set[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(conv2d_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ConvCfg<BN>::SMEM_BYTES);
+        e = cudaFuncSetAttribute(conv2d_tc_kernel<PBN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
-    const long long m_tiles = static_cast<long long>(s.B) * ((s.HO + s.rows - 1) / s.rows) * ((s.WO + s.tile_w - 1) / s.tile_w);
-    dim3 grid(static_cast<unsigned>(m_tiles), (s.F + BN - 1) / BN);
-    conv2d_tc_kernel<BN><<<grid, NUM_THREADS, ConvCfg<BN>::SMEM_BYTES, stream>>>(tm_x, tm_w, out, bias, s, status);
+    const long long num_tiles = ((conv_tc_rows(s) + PBM - 1) / PBM) * ((s.F + PBN - 1) / PBN);
+    const long long max_pairs = num_sms / 2 > 0 ? num_sms / 2 : 1;
+    const int pairs = static_cast<int>(num_tiles < max_pairs ? num_tiles : max_pairs);
+    // float4 stores need 16-byte aligned output rows and 4-pixel groups that never straddle a padded row
+    const int xwp = conv_tc_xwp(s);
+    const int vec_ok = (s.WO % 4) == 0 && (xwp % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+    conv2d_tc_kernel<PBN><<<2 * pairs, NUM_THREADS, smem, stream>>>(tm_x, tm_w, out, bias, s, vec_ok, status);
     return cudaGetLastError();
 }
 
 }  // namespace
 
 bool conv2d_tc_supported(const ConvTcShape& s) {
-    return s.sh == 1 && s.sw == 1 && s.B > 0 && s.F > 0 && s.Cp % 8 == 0 && s.tile_w > 0 && s.rows > 0 && s.tile_w * s.rows <= BM &&
-           static_cast<long long>(s.B) * ((s.HO + s.rows - 1) / s.rows) * ((s.WO + s.tile_w - 1) / s.tile_w) < (1LL << 31);
+    const long long xhp = conv_tc_xhp(s), xwp = conv_tc_xwp(s);
+    const long long max_shift = static_cast<long long>(s.KH - 1) * s.dh * xwp + static_cast<long long>(s.KW - 1) * s.dw;
+    const long long rows = conv_tc_rows(s);
+    const long long tiles = (rows + PBM - 1) / PBM * ((s.F + 63) / 64);
+    return s.sh == 1 && s.sw == 1 && s.B > 0 && s.F > 0 && s.Cp > 0 && s.Cp % 8 == 0 && xhp > 0 && xwp > 0 &&
+           rows + PBM + max_shift < (1LL << 31) && tiles < (1LL << 31) && (s.Cp + 63) / 64 <= 65535;
 }
 
-int conv2d_tc_block_n(int F) { return F <= 32 ? 32 : (F <= 64 ? 64 : 128); }
+int conv2d_tc_block_n(int F) { return F <= 64 ? 64 : (F <= 128 ? 128 : 256); }
 
-cudaError_t conv2d_tc_repack(__nv_bfloat16* x_nhwc, __nv_bfloat16* w_ftc, const __nv_bfloat16* input, const __nv_bfloat16* weight,
-                             const ConvTcShape& s, cudaStream_t stream) {
-    const int HW = s.XH * s.XW;
-    dim3 tgrid((HW + 31) / 32, (s.Cp + 31) / 32, s.B);
-    nchw_to_nhwc_kernel<<<tgrid, dim3(32, 8), 0, stream>>>(x_nhwc, input, s.C, s.Cp, HW);
+size_t conv2d_tc_weight_offset(const ConvTcShape& s) {
+    return (static_cast<size_t>(conv_tc_rows(s)) * s.Cp * 2 + 255) & ~size_t(255);
+}
+
+size_t conv2d_tc_scratch_bytes(const ConvTcShape& s) {
+    return conv2d_tc_weight_offset(s) + static_cast<size_t>(s.F) * s.KH * s.KW * s.Cp * 2;
+}
+
+cudaError_t conv2d_tc_repack(void* scratch, const __nv_bfloat16* input, const __nv_bfloat16* weight, const ConvTcShape& s,
+                             cudaStream_t stream) {
+    __nv_bfloat16* x_pad = static_cast<__nv_bfloat16*>(scratch);
+    __nv_bfloat16* w_ftc = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(scratch) + conv2d_tc_weight_offset(s));
+    const long long planes = static_cast<long long>(s.B) * conv_tc_xhp(s);
+    if (planes >= (1LL << 31)) return cudaErrorInvalidValue;
+    const int vec_ok = (s.XW % 8) == 0 && (reinterpret_cast<uintptr_t>(input) & 15u) == 0;
+    dim3 tgrid(static_cast<unsigned>(planes), (s.Cp + RP_CH - 1) / RP_CH);
+    nchw_to_padded_nhwc_kernel<<<tgrid, 256, 0, stream>>>(x_pad, input, s, vec_ok);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const long long wtotal = static_cast<long long>(s.F) * s.KH * s.KW * s.Cp;
+    const long long wtotal = static_cast<long long>(s.F) * s.Cp;
     const int blocks = static_cast<int>((wtotal + 255) / 256 < 4096 ? (wtotal + 255) / 256 : 4096);
     weight_to_ftc_kernel<<<blocks, 256, 0, stream>>>(w_ftc, weight, s.F, s.C, s.Cp, s.KH * s.KW);
     return cudaGetLastError();
 }
 
 cudaError_t conv2d_tc_launch(const CUtensorMap& tm_x, const CUtensorMap& tm_w, float* out, const float* bias, const ConvTcShape& s,
-                             int* status, cudaStream_t stream) {
+                             int num_sms, int* status, cudaStream_t stream) {
     switch (conv2d_tc_block_n(s.F)) {
-        case 32: return launch_bn<32>(tm_x, tm_w, out, bias, s, status, stream);
-        case 64: return launch_bn<64>(tm_x, tm_w, out, bias, s, status, stream);
-        default: return launch_bn<128>(tm_x, tm_w, out, bias, s, status, stream);
+        case 64: return launch_pbn<64>(tm_x, tm_w, out, bias, s, num_sms, status, stream);
+        case 128: return launch_pbn<128>(tm_x, tm_w, out, bias, s, num_sms, status, stream);
+        default: return launch_pbn<256>(tm_x, tm_w, out, bias, s, num_sms, status, stream);
     }
 }
 

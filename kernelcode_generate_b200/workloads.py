@@ -47,6 +47,18 @@ CONFIGS: dict[str, Config] = {
                  _fa_flops(4, 32, 8192, 128, True), (128, 128), "flash attention bf16 causal 4x32x8192x128, scale 1/sqrt(128)"),
 }
 
+# Extension workloads: not BASELINE configurations; measured beside them to show a kernel the five
+# configurations do not reach. X1 is the bf16 tensor-core conv2d on the shape of VGG-16's conv3_2
+# layer (256 -> 256 channels, 3x3, pad 1, 56x56) at batch 32, sharded by batch like north_star's conv2d.
+EXTENSION_CONFIGS: dict[str, Config] = {
+    "X1": Config("X1", "conv2d", "bf16", dict(B=32, C=256, XH=56, XW=56, F=256, KH=3, KW=3, stride=(1, 1), dilation=(1, 1),
+                                               pads=(1, 1, 1, 1)), 5, 2 * 32 * 256 * 56 * 56 * 256 * 9, (16, 64, 16, 8, 56),
+                 "extension (not a BASELINE config): conv2d bf16 NCHW 32x256x56x56 -> 256, 3x3 s1 p1 (VGG-16 conv3_2 shape), "
+                 "x ~ U(-1,1), w ~ N(0, 1/144)"),
+}
+
+ALL_CONFIGS: dict[str, Config] = {**CONFIGS, **EXTENSION_CONFIGS}
+
 
 def bf16_bits(a: np.ndarray) -> np.ndarray:
     """fp32 -> bf16 (round to nearest even), as uint16 bit patterns."""
@@ -61,7 +73,7 @@ def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
 def make_inputs(cfg: Config | str) -> dict[str, np.ndarray]:
     """Seeded host inputs for a configuration (f32 arrays; bf16 configs as uint16 bits)."""
     if isinstance(cfg, str):
-        cfg = CONFIGS[cfg]
+        cfg = ALL_CONFIGS[cfg]
     rng = np.random.default_rng(cfg.seed)
     s = cfg.shape
     if cfg.kernel == "matmul":
@@ -75,6 +87,8 @@ def make_inputs(cfg: Config | str) -> dict[str, np.ndarray]:
     if cfg.kernel == "conv2d":
         x = rng.uniform(-1.0, 1.0, (s["B"], s["C"], s["XH"], s["XW"])).astype(np.float32)
         w = (rng.standard_normal((s["F"], s["C"], s["KH"], s["KW"]), dtype=np.float32) / np.float32(12.0)).astype(np.float32)
+        if cfg.dtype == "bf16":
+            return {"input": bf16_bits(x), "weight": bf16_bits(w)}
         return {"input": x, "weight": w}
     shape = (s["B"], s["H"], s["S"], s["D"])
     q = rng.standard_normal(shape, dtype=np.float32)
