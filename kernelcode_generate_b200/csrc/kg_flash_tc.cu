@@ -8,11 +8,15 @@
 // CTA work unit: one (b, h) and two 128-row query tiles Q0, Q1 (256 rows). Key/value tiles of 128
 // rows stream through a 2-stage TMA ring. TMEM (512 columns): S0 | S1 | O0 | O1; P_i (bf16) is
 // written back over the first half of S_i's columns and consumed from TMEM by the PV MMA.
-//   warps 0-3   softmax + epilogue for Q0 (thread = query row = TMEM lane)
-//   warps 4-7   softmax + epilogue for Q1
-//   warp 8      TMA producer (Q once; K_j, V_j per key tile)
-//   warp 9      MMA issuer (S_i = Q_i K_j^T; O_i += P_i V_j), ping-ponging the two tiles so the
+//   warp 0      MMA issuer (S_i = Q_i K_j^T; O_i += P_i V_j), ping-ponging the two tiles so the
 //               tensor core works on one tile while the other tile's softmax runs
+//   warp 1      TMA producer (Q once; K_j, V_j per key tile)
+//   warps 2-3   idle (they complete the first warpgroup, whose registers go to the softmax)
+//   warps 4-7   softmax + epilogue for Q0 (thread = query row = TMEM lane)
+//   warps 8-11  softmax + epilogue for Q1
+// The MMA warp shares a scheduler with two softmax warps. Measured on B200, a warp's share of a
+// busy scheduler's issue slots depends on its id and warp 0 fares best, so the warp whose
+// instructions gate the tensor core gets that id.
 // The running max is only moved when it grows by more than 2^8 (log2 domain); O and l keep using
 // the stale max otherwise, which is exact because both are scaled by the same factor.
 #include "kg_flash_tc.h"
@@ -24,7 +28,14 @@ namespace {
 constexpr int BM = 128;          // query rows per tile (TMEM lanes)
 constexpr int BN = 128;          // key rows per tile
 constexpr int KV_STAGES = 2;
-constexpr int NUM_THREADS = 320; // 10 warps
+constexpr int NUM_THREADS = 384; // 12 warps = 3 warpgroups
+// Register budgets after the prologue: the two softmax warpgroups keep a row of scores (128 f32)
+// plus its packed P in registers; the producer/MMA warpgroup needs few. Their sum equals the
+// launch allocation, 384 threads x 168 registers (checked by the launcher).
+constexpr uint32_t SOFTMAX_REGS = 208;
+constexpr uint32_t CONTROL_REGS = 80;
+constexpr int LAUNCH_REGS = 168;
+static_assert(2 * 128 * SOFTMAX_REGS + 128 * CONTROL_REGS <= NUM_THREADS * LAUNCH_REGS, "register split exceeds the launch budget");
 constexpr float RESCALE_THRESHOLD = 8.0f;
 
 template <int D>
@@ -61,8 +72,12 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-#ifndef KG_FA_POLY_PAIRS
-#define KG_FA_POLY_PAIRS 0
+// Of every 4 score pairs, this many take 2^x from the FMA-pipe polynomial instead of the MUFU ex2
+// unit. With D = 128 the MUFU needs as many cycles per key tile as the tile's MMAs, but the
+// polynomial's ~10 extra instructions per pair also compete for the issue slots the MMA warp
+// needs; on B200 every non-zero setting measured slower on C5 (1 of 4: -4 %, 2 of 4: -10 %).
+#ifndef KG_FA_POLY_PER4
+#define KG_FA_POLY_PER4 0
 #endif
 
 __device__ __forceinline__ float max3(float a, float b, float c) {
@@ -183,7 +198,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         bars->abort = 0;
         fence_barrier_init();
     }
-    if (warp == 9) {
+    if (warp == 0) {
         tmem_alloc(&bars->tmem_base, Cfg::TMEM_COLS);
         tmem_relinquish();
     }
@@ -192,121 +207,136 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
     volatile int* abort = &bars->abort;
-
-    if (warp == 8) {
-        // ------------------------------------------------------------ TMA producer
-        if (lane == 0) {
-            tma_prefetch_desc(&tm_q);
-            tma_prefetch_desc(&tm_k);
-            tma_prefetch_desc(&tm_v);
-            mbar_arrive_expect_tx(&bars->q_full, 2 * Cfg::Q_TILE_BYTES);
-            for (int i = 0; i < 2; ++i)
-                for (int db = 0; db < Cfg::DBLK; ++db)
-                    tma_load_3d(sQ + i * Cfg::Q_TILE_BYTES + db * Cfg::TILE_BLOCK_BYTES, &tm_q, &bars->q_full, db * 64, m0 + i * BM, bh);
-            int issued = 0;
-            for (int j = 0; j < n_max && !*abort; ++j) {
-                const int st = j % KV_STAGES;
-                const uint32_t ph = (j / KV_STAGES) & 1u;
-                if (!mbar_wait(&bars->k_empty[st], ph ^ 1u, abort, status, kDevTimeoutProducer)) break;
-                mbar_arrive_expect_tx(&bars->k_full[st], Cfg::KV_TILE_BYTES);
-                for (int db = 0; db < Cfg::DBLK; ++db)
-                    tma_load_3d(sK + st * Cfg::KV_TILE_BYTES + db * Cfg::TILE_BLOCK_BYTES, &tm_k, &bars->k_full[st], db * 64, j * BN, bh);
-                if (!mbar_wait(&bars->v_empty[st], ph ^ 1u, abort, status, kDevTimeoutProducer)) break;
-                mbar_arrive_expect_tx(&bars->v_full[st], Cfg::KV_TILE_BYTES);
-                for (int db = 0; db < Cfg::DBLK; ++db)
-                    tma_load_3d(sV + st * Cfg::KV_TILE_BYTES + db * Cfg::TILE_BLOCK_BYTES, &tm_v, &bars->v_full[st], db * 64, j * BN, bh);
-                issued = j + 1;
-            }
-            if (*abort) {
-                int keep_waiting = 0;
-                mbar_wait(&bars->q_full, 0, &keep_waiting, nullptr, 0);
-                for (int j = max(0, issued - KV_STAGES); j < issued; ++j) {
+    if (warp < 4) {
+        setmaxnreg_dec<CONTROL_REGS>();
+        if (warp == 1) {
+            // ------------------------------------------------------------ TMA producer
+            if (lane == 0) {
+                tma_prefetch_desc(&tm_q);
+                tma_prefetch_desc(&tm_k);
+                tma_prefetch_desc(&tm_v);
+                mbar_arrive_expect_tx(&bars->q_full, 2 * Cfg::Q_TILE_BYTES);
+                for (int i = 0; i < 2; ++i)
+                    for (int db = 0; db < Cfg::DBLK; ++db)
+                        tma_load_3d(sQ + i * Cfg::Q_TILE_BYTES + db * Cfg::TILE_BLOCK_BYTES, &tm_q, &bars->q_full, db * 64, m0 + i * BM, bh);
+                int issued = 0;
+                for (int j = 0; j < n_max && !*abort; ++j) {
                     const int st = j % KV_STAGES;
                     const uint32_t ph = (j / KV_STAGES) & 1u;
-                    mbar_wait(&bars->k_full[st], ph, &keep_waiting, nullptr, 0);
-                    mbar_wait(&bars->v_full[st], ph, &keep_waiting, nullptr, 0);
+                    if (!mbar_wait(&bars->k_empty[st], ph ^ 1u, abort, status, kDevTimeoutProducer)) break;
+                    mbar_arrive_expect_tx(&bars->k_full[st], Cfg::KV_TILE_BYTES);
+                    for (int db = 0; db < Cfg::DBLK; ++db)
+                        tma_load_3d(sK + st * Cfg::KV_TILE_BYTES + db * Cfg::TILE_BLOCK_BYTES, &tm_k, &bars->k_full[st], db * 64, j * BN, bh);
+                    if (!mbar_wait(&bars->v_empty[st], ph ^ 1u, abort, status, kDevTimeoutProducer)) break;
+                    mbar_arrive_expect_tx(&bars->v_full[st], Cfg::KV_TILE_BYTES);
+                    for (int db = 0; db < Cfg::DBLK; ++db)
+                        tma_load_3d(sV + st * Cfg::KV_TILE_BYTES + db * Cfg::TILE_BLOCK_BYTES, &tm_v, &bars->v_full[st], db * 64, j * BN, bh);
+                    issued = j + 1;
                 }
-            }
-        }
-    } else if (warp == 9) {
-        // ------------------------------------------------------------ MMA issuer
-        const uint32_t q_base = smem_u32(sQ);
-        const uint32_t k_base = smem_u32(sK);
-        const uint32_t v_base = smem_u32(sV);
-        auto issue_s = [&](int i, int j) {
-            const int st = j % KV_STAGES;
-            if (lane == 0) {
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t koff = (kk / 4) * Cfg::TILE_BLOCK_BYTES + (kk % 4) * 32;
-                    const uint64_t a = smem_desc_sw128(q_base + i * Cfg::Q_TILE_BYTES + koff, 16, 1024);
-                    const uint64_t b = smem_desc_sw128(k_base + st * Cfg::KV_TILE_BYTES + koff, 16, 1024);
-                    umma_f16(tmem + Cfg::s_col(i), a, b, Cfg::IDESC_S, kk > 0 ? 1u : 0u);
-                }
-                umma_commit(&bars->s_ready[i]);
-            }
-            __syncwarp();
-        };
-        auto issue_pv = [&](int i, int j) {
-            const int st = j % KV_STAGES;
-            if (lane == 0) {
-#pragma unroll
-                for (int kk = 0; kk < BN / 16; ++kk) {
-                    const uint64_t b = smem_desc_sw128(v_base + st * Cfg::KV_TILE_BYTES + kk * 2048, Cfg::TILE_BLOCK_BYTES, 1024);
-                    umma_f16_ts(tmem + Cfg::o_col(i), tmem + Cfg::s_col(i) + kk * 8, b, Cfg::IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
-                }
-            }
-            __syncwarp();
-        };
-        auto commit = [&](uint64_t* bar) {
-            if (lane == 0) umma_commit(bar);
-            __syncwarp();
-        };
-        bool ok = mbar_wait(&bars->q_full, 0, abort, status, kDevTimeoutMma);
-        if (ok && n_max > 0) {
-            ok = mbar_wait(&bars->k_full[0], 0, abort, status, kDevTimeoutMma);
-            if (ok) {
-                tc_fence_after();
-#pragma unroll
-                for (int i = 0; i < 2; ++i)
-                    if (n_tiles(i) > 0) issue_s(i, 0);
-                commit(&bars->k_empty[0]);
-            }
-        }
-        for (int j = 0; ok && j < n_max; ++j) {
-            const int st = j % KV_STAGES;
-            const uint32_t ph = (j / KV_STAGES) & 1u;
-            const int nst = (j + 1) % KV_STAGES;
-            const uint32_t nph = ((j + 1) / KV_STAGES) & 1u;
-            if (!(ok = mbar_wait(&bars->v_full[st], ph, abort, status, kDevTimeoutMma))) break;
-            bool next_k_loaded = false;
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                if (j >= n_tiles(i)) continue;
-                if (!(ok = mbar_wait(&bars->p_ready[i], j & 1u, abort, status, kDevTimeoutMma))) break;
-                tc_fence_after();
-                issue_pv(i, j);
-                if (j + 1 < n_tiles(i)) {
-                    if (!next_k_loaded) {
-                        if (!(ok = mbar_wait(&bars->k_full[nst], nph, abort, status, kDevTimeoutMma))) break;
-                        tc_fence_after();
-                        next_k_loaded = true;
+                if (*abort) {
+                    int keep_waiting = 0;
+                    mbar_wait(&bars->q_full, 0, &keep_waiting, nullptr, 0);
+                    for (int j = max(0, issued - KV_STAGES); j < issued; ++j) {
+                        const int st = j % KV_STAGES;
+                        const uint32_t ph = (j / KV_STAGES) & 1u;
+                        mbar_wait(&bars->k_full[st], ph, &keep_waiting, nullptr, 0);
+                        mbar_wait(&bars->v_full[st], ph, &keep_waiting, nullptr, 0);
                     }
-                    issue_s(i, j + 1);
-                } else {
-                    commit(&bars->o_done[i]);
                 }
             }
-            if (!ok) break;
-            commit(&bars->v_empty[st]);
-            if (next_k_loaded) commit(&bars->k_empty[nst]);
+        } else if (warp == 0) {
+            // ------------------------------------------------------------ MMA issuer
+            // The MMA warp shares its scheduler with two softmax warps, which keep it busy; every
+            // instruction it needs per MMA delays the tensor core. So the shared-memory descriptors
+            // are built once and stepped by constants (the start-address field is the low 14 bits,
+            // in 16-byte units, and never carries: shared addresses are below 256 KB).
+            const uint64_t q_desc0 = smem_desc_sw128(smem_u32(sQ), 16, 1024);
+            const uint64_t q_desc1 = smem_desc_sw128(smem_u32(sQ) + Cfg::Q_TILE_BYTES, 16, 1024);
+            const uint64_t k_desc0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
+            const uint64_t k_desc1 = smem_desc_sw128(smem_u32(sK) + Cfg::KV_TILE_BYTES, 16, 1024);
+            const uint64_t v_desc0 = smem_desc_sw128(smem_u32(sV), Cfg::TILE_BLOCK_BYTES, 1024);
+            const uint64_t v_desc1 = smem_desc_sw128(smem_u32(sV) + Cfg::KV_TILE_BYTES, Cfg::TILE_BLOCK_BYTES, 1024);
+            auto issue_s = [&](int i, int j) {
+                if (lane == 0) {
+                    const uint64_t qd = i == 0 ? q_desc0 : q_desc1;
+                    const uint64_t kd = (j % KV_STAGES) == 0 ? k_desc0 : k_desc1;
+                    const uint32_t d = tmem + Cfg::s_col(i);
+#pragma unroll
+                    for (int kk = 0; kk < D / 16; ++kk) {
+                        const uint64_t off = static_cast<uint64_t>(((kk / 4) * Cfg::TILE_BLOCK_BYTES + (kk % 4) * 32) >> 4);
+                        umma_f16(d, qd + off, kd + off, Cfg::IDESC_S, kk > 0 ? 1u : 0u);
+                    }
+                    umma_commit(&bars->s_ready[i]);
+                }
+                __syncwarp();
+            };
+            auto issue_pv = [&](int i, int j) {
+                if (lane == 0) {
+                    const uint64_t vd = (j % KV_STAGES) == 0 ? v_desc0 : v_desc1;
+                    const uint32_t d = tmem + Cfg::o_col(i);
+                    const uint32_t a = tmem + Cfg::s_col(i);
+                    if (j > 0) {
+#pragma unroll
+                        for (int kk = 0; kk < BN / 16; ++kk) umma_f16_ts(d, a + kk * 8, vd + static_cast<uint64_t>(kk * 128), Cfg::IDESC_O, 1u);
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < BN / 16; ++kk)
+                            umma_f16_ts(d, a + kk * 8, vd + static_cast<uint64_t>(kk * 128), Cfg::IDESC_O, kk > 0 ? 1u : 0u);
+                    }
+                }
+                __syncwarp();
+            };
+            auto commit = [&](uint64_t* bar) {
+                if (lane == 0) umma_commit(bar);
+                __syncwarp();
+            };
+            bool ok = mbar_wait(&bars->q_full, 0, abort, status, kDevTimeoutMma);
+            if (ok && n_max > 0) {
+                ok = mbar_wait(&bars->k_full[0], 0, abort, status, kDevTimeoutMma);
+                if (ok) {
+                    tc_fence_after();
+    #pragma unroll
+                    for (int i = 0; i < 2; ++i)
+                        if (n_tiles(i) > 0) issue_s(i, 0);
+                    commit(&bars->k_empty[0]);
+                }
+            }
+            for (int j = 0; ok && j < n_max; ++j) {
+                const int st = j % KV_STAGES;
+                const uint32_t ph = (j / KV_STAGES) & 1u;
+                const int nst = (j + 1) % KV_STAGES;
+                const uint32_t nph = ((j + 1) / KV_STAGES) & 1u;
+                if (!(ok = mbar_wait(&bars->v_full[st], ph, abort, status, kDevTimeoutMma))) break;
+                bool next_k_loaded = false;
+    #pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    if (j >= n_tiles(i)) continue;
+                    if (!(ok = mbar_wait(&bars->p_ready[i], j & 1u, abort, status, kDevTimeoutMma))) break;
+                    tc_fence_after();
+                    issue_pv(i, j);
+                    if (j + 1 < n_tiles(i)) {
+                        if (!next_k_loaded) {
+                            if (!(ok = mbar_wait(&bars->k_full[nst], nph, abort, status, kDevTimeoutMma))) break;
+                            tc_fence_after();
+                            next_k_loaded = true;
+                        }
+                        issue_s(i, j + 1);
+                    } else {
+                        commit(&bars->o_done[i]);
+                    }
+                }
+                if (!ok) break;
+                commit(&bars->v_empty[st]);
+                if (next_k_loaded) commit(&bars->k_empty[nst]);
+            }
+            commit(&bars->drain);
+            int keep_waiting = 0;
+            mbar_wait(&bars->drain, 0, &keep_waiting, status, kDevTimeoutDrain);
         }
-        commit(&bars->drain);
-        int keep_waiting = 0;
-        mbar_wait(&bars->drain, 0, &keep_waiting, status, kDevTimeoutDrain);
     } else {
-        // ------------------------------------------------------------ softmax + epilogue (warps 0-7)
-        const int i = warp >> 2;            // query tile of this warpgroup
+        setmaxnreg_inc<SOFTMAX_REGS>();
+        // ------------------------------------------------------------ softmax + epilogue (warps 4-11)
+        const int i = (warp >> 2) - 1;      // query tile of this warpgroup
         const int quarter = warp & 3;       // TMEM lane quarter
         const int r = quarter * 32 + lane;  // row within the tile
         const int q0 = m0 + i * BM;
@@ -337,11 +367,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                 for (int t = 0; t < BN; ++t) sc[t] = t < lim ? sc[t] : -INFINITY;
             }
-            // Row maximum of the raw scores (scale_log2 > 0, so it commutes with the scaling).
-            float mx = max3(sc[0], sc[1], sc[2]);
+            // Row maximum of the raw scores (scale_log2 > 0, so it commutes with the scaling): eight
+            // independent partial maxima over 16 columns each, then combined.
+            float m8[8];
 #pragma unroll
-            for (int t = 3; t + 1 < BN; t += 2) mx = max3(mx, sc[t], sc[t + 1]);
-            mx = fmaxf(mx, sc[BN - 1]);
+            for (int g = 0; g < 8; ++g) {
+                float mg = max3(sc[16 * g], sc[16 * g + 1], sc[16 * g + 2]);
+#pragma unroll
+                for (int t = 3; t + 1 < 16; t += 2) mg = max3(mg, sc[16 * g + t], sc[16 * g + t + 1]);
+                m8[g] = fmaxf(mg, sc[16 * g + 15]);
+            }
+            float mx = max3(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
             mx *= scale_log2;
             float alpha = 1.0f;
             bool rescale_o = false;
@@ -355,11 +391,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
             // P = 2^(s * scale_log2 - m) as bf16, written over the first half of S's columns (chunk c
-            // writes columns 16c..16c+15, already read above). KG_FA_POLY_PAIRS of every 16 pairs use
-            // the FMA-pipe polynomial instead of the MUFU ex2 unit, which is the softmax bottleneck.
+            // writes columns 16c..16c+15, already read above); the f32 values stay in sc for the row sum,
+            // which is formed after P has been handed over.
             const uint64_t scale2 = pack_f32x2(scale_log2, scale_log2);
             const uint64_t negm2 = pack_f32x2(-m_use, -m_use);
-            uint64_t sum2 = pack_f32x2(0.0f, 0.0f);
 #pragma unroll
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t pk[16];
@@ -369,21 +404,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     float x0, x1;
                     unpack_f32x2(x2, x0, x1);
                     float p0, p1;
-                    if (t < KG_FA_POLY_PAIRS) {
+                    if ((t & 3) < KG_FA_POLY_PER4) {
                         exp2_poly2(x0, x1, p0, p1);
                     } else {
                         p0 = ex2(x0);
                         p1 = ex2(x1);
                     }
-                    sum2 = add_f32x2(sum2, pack_f32x2(p0, p1));
+                    sc[c * 32 + 2 * t] = p0;
+                    sc[c * 32 + 2 * t + 1] = p1;
                     pk[t] = pack_bf16(p0, p1);
                 }
                 tmem_st_32x32b_x16(s_addr + c * 16, pk);
             }
-            float sum_lo, sum_hi;
-            unpack_f32x2(sum2, sum_lo, sum_hi);
-            const float sum = sum_lo + sum_hi;
-            l_run = l_run * alpha + sum;
             if (rescale_o) {
                 // s_ready(j) implies PV(j-1) has completed (tcgen05 ops complete in issue order).
 #pragma unroll 1
@@ -404,6 +436,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(&bars->p_ready[i]);
+            // Row sum of P (f32), off the tensor core's critical path; four independent partial sums.
+            uint64_t sum2[4] = {pack_f32x2(0.0f, 0.0f), pack_f32x2(0.0f, 0.0f), pack_f32x2(0.0f, 0.0f), pack_f32x2(0.0f, 0.0f)};
+#pragma unroll
+            for (int t = 0; t < BN / 2; ++t) sum2[t & 3] = add_f32x2(sum2[t & 3], pack_f32x2(sc[2 * t], sc[2 * t + 1]));
+            float sum_lo, sum_hi;
+            unpack_f32x2(add_f32x2(add_f32x2(sum2[0], sum2[1]), add_f32x2(sum2[2], sum2[3])), sum_lo, sum_hi);
+            l_run = l_run * alpha + (sum_lo + sum_hi);
         }
         // epilogue: O / l -> bf16 -> global
         if (n > 0 && !*abort) {
@@ -434,7 +473,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 9) {
+    if (warp == 0) {
         tmem_dealloc(tmem, Cfg::TMEM_COLS);
     }
 }
@@ -475,6 +514,12 @@ cudaError_t flash_fwd_tc_launch(const CUtensorMap& tm_q, const CUtensorMap& tm_k
                     : cudaFuncSetAttribute(flash_fwd_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            (int)FlashCfg<128>::SMEM_BYTES);
         if (e != cudaSuccess) return e;
+        // The warpgroups' setmaxnreg budgets assume LAUNCH_REGS registers per thread at launch; with
+        // fewer, the softmax warpgroups' increase could never be granted, so refuse to launch.
+        cudaFuncAttributes fa{};
+        e = D == 64 ? cudaFuncGetAttributes(&fa, flash_fwd_tc_kernel<64>) : cudaFuncGetAttributes(&fa, flash_fwd_tc_kernel<128>);
+        if (e != cudaSuccess) return e;
+        if (fa.numRegs != LAUNCH_REGS) return cudaErrorInvalidConfiguration;
         if (dev >= 0 && dev < 64) attr_set[which][dev] = true;
     }
     if (D == 64) {
