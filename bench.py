@@ -28,6 +28,8 @@ from pathlib import Path
 
 import numpy as np
 
+from kernelcode_generate_b200.sharding import gather_rows, shard_range
+
 ROOT = Path(__file__).resolve().parent
 METRIC = "TFLOP/s and % of B200 tensor peak for matmul/conv2d/flash-attn at 1/2/4/8 GPU"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -45,6 +47,9 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
+    ap.add_argument("--gather", action="store_true",
+                    help="after the timed loop, all-gather the sharded output into one tensor per rank (NCCL) and time it; "
+                         "not part of the metric")
     return ap.parse_args(argv)
 
 
@@ -179,8 +184,6 @@ def to_device(x, dev):
     return torch.from_numpy(x).to(dev)
 
 
-def shard_range(total: int, rank: int, world: int):
-    return total * rank // world, total * (rank + 1) // world
 
 
 class Workload:
@@ -263,6 +266,32 @@ def time_steps(wl, steps, warmup, world, flush):
     if runtime.device_status() != 0:
         raise RuntimeError("a kernel reported a pipeline timeout during the timed region")
     return reduce_max(total, world), total / steps, kernel
+
+
+def gather_run(cfg, wl, world):
+    """All-gathers the rank's output block into the full output tensor on every rank (the
+    single-tensor result north_star allows NCCL for); returns its time, max over ranks."""
+    import torch
+
+    s = cfg.shape
+    if cfg.kernel == "matmul":
+        local, total = wl.out, s["M"]
+    elif cfg.kernel == "flash_attention":
+        local, total = wl.out.reshape(-1, s["S"], s["D"]), s["B"] * s["H"]
+    elif s["B"] >= world:
+        local, total = wl.out, s["B"]
+    else:
+        return None  # replicas: every rank already holds the whole result
+    stream = torch.cuda.current_stream()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    start.record(stream)
+    full = gather_rows(local, total)
+    end.record(stream)
+    barrier(world)
+    ms = reduce_max(start.elapsed_time(end), world)
+    return {"ms": round(ms, 4), "bytes": int(full.numel() * full.element_size()), "collective": "all_gather_into_tensor (NCCL)",
+            "shape": list(full.shape)}
 
 
 def _pinned(x):
@@ -398,9 +427,9 @@ def reference_arm(args):
 
 
 def launches_per_step(kernel: str) -> int:
-    """Kernels of this library one step launches: the tensor-core conv2d repacks its input and
-    weights (two kernels) before the GEMM kernel; every other path is one kernel."""
-    return 3 if kernel == "conv2d_tc_kernel" else 1
+    """Kernels of this library one step launches: the tensor-core conv2d runs one repack kernel
+    (input and weights) before the GEMM kernel; every other path is one kernel."""
+    return 2 if kernel == "conv2d_tc_kernel" else 1
 
 
 def workload_config(cfg, n_gpus):
@@ -435,6 +464,7 @@ def main(argv=None):
     achieved = wl.flops / (launch_ms * 1e-3) / 1e12  # this rank's kernel, algorithmic FLOPs per launch
     tensor_peak = peaks["bf16_tflops"]
     traffic = load_traffic(kernel, cfg.name)
+    gather = gather_run(cfg, wl, world) if args.gather and world > 1 else None
     e2e = None
     if not args.no_e2e:
         e2e = e2e_run(cfg, wl, args.e2e_steps, world)
@@ -480,6 +510,8 @@ def main(argv=None):
             "clocks": clocks.summary(),
             "suite": suite,
         }
+        if gather is not None:
+            line["gather"] = gather
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

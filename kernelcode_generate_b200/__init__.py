@@ -6,6 +6,7 @@ Layers:
     execute_engine   ExecutionEngine / CompiledKernel for target "cuda_sm100" (reference facade)
     kernels          the three kernels as Python callables (slot ABI and typed entries)
     workloads        the benchmark configurations and their seeded inputs
+    sharding         the per-rank partition of each kernel and the optional output all-gather
 """
 
 from .runtime import KernelBackendUnavailable, KernelError, load  # noqa: F401

@@ -8,6 +8,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -390,7 +391,9 @@ struct Staging {
 };
 std::vector<Staging> g_staging;
 
-int stage_in(std::vector<MemArg*>& args, cudaStream_t stream) {
+// Host-memory arguments get device copies in a per-device staging arena (`stage_alloc` assigns
+// them device space; nothing is copied).
+int stage_alloc(std::vector<MemArg*>& args) {
     size_t total = 0;
     for (MemArg* m : args) {
         if (m->data == nullptr) continue;
@@ -422,8 +425,39 @@ int stage_in(std::vector<MemArg*>& args, cudaStream_t stream) {
         if (m->data == nullptr || !m->host) continue;
         m->dev = static_cast<char*>(st.ptr) + off;
         off += (m->bytes + 255) & ~size_t(255);
-        KG_CUDA_TRY(cudaMemcpyAsync(m->dev, m->data, m->bytes, cudaMemcpyHostToDevice, stream));
     }
+    return KG_OK;
+}
+
+// Three non-blocking streams per device for calls whose operands are all in host memory: uploads,
+// kernels and downloads of successive row blocks overlap (the copy engines run both directions at
+// once while the GPU computes).
+constexpr int kPipeMaxChunks = 16;
+struct Pipe {
+    cudaStream_t up = nullptr, compute = nullptr, down = nullptr;
+    cudaEvent_t uploaded[kPipeMaxChunks] = {};
+    cudaEvent_t computed[kPipeMaxChunks] = {};
+    cudaEvent_t operands = nullptr;
+};
+std::vector<Pipe> g_pipes;
+
+int get_pipe(Pipe** out) {
+    int dev = 0;
+    KG_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (static_cast<int>(g_pipes.size()) <= dev) g_pipes.resize(dev + 1);
+    Pipe& p = g_pipes[dev];
+    if (p.up == nullptr) {
+        KG_CUDA_TRY(cudaStreamCreateWithFlags(&p.up, cudaStreamNonBlocking));
+        KG_CUDA_TRY(cudaStreamCreateWithFlags(&p.compute, cudaStreamNonBlocking));
+        KG_CUDA_TRY(cudaStreamCreateWithFlags(&p.down, cudaStreamNonBlocking));
+        KG_CUDA_TRY(cudaEventCreateWithFlags(&p.operands, cudaEventDisableTiming));
+        for (int i = 0; i < kPipeMaxChunks; ++i) {
+            KG_CUDA_TRY(cudaEventCreateWithFlags(&p.uploaded[i], cudaEventDisableTiming));
+            KG_CUDA_TRY(cudaEventCreateWithFlags(&p.computed[i], cudaEventDisableTiming));
+        }
+    }
+    *out = &p;
     return KG_OK;
 }
 
@@ -444,6 +478,75 @@ int finish_call(int rc, MemArg* out, cudaStream_t stream) {
         cudaMemcpy(dev->status, &zero, sizeof(int), cudaMemcpyHostToDevice);
         return fail(KG_ERR_DEVICE_TIMEOUT, "kernel %s reported device status %d (pipeline wait timed out)", g_last_kernel, code);
     }
+    return KG_OK;
+}
+
+// Host-buffer calls in row blocks. The operands that every block needs (`whole`) go up first; then
+// per block of rows along the partitioned dimension the block's input rows go up, `launch` runs the
+// kernel on them and the block's output rows come down, on three streams so that block i's
+// download, block i+1's kernel and block i+2's upload overlap. The kernels compute every output
+// row the same way whatever rows surround it, so the result is the same bit for bit as one launch.
+struct RowArg {
+    MemArg* arg;
+    size_t row_bytes;  // bytes of one row along the partitioned dimension
+};
+constexpr long long kPipeRowBlock = 256;  // matmul row blocks are whole 256-row pair tiles
+constexpr size_t kPipeMinBytes = 32u << 20;
+
+bool pipeline_worth_it(const std::vector<RowArg>& in, const RowArg& out, long long rows) {
+    if (!out.arg->host || rows < 2) return false;
+    size_t bytes = out.row_bytes * rows;
+    for (const RowArg& r : in) {
+        if (!r.arg->host) return false;
+        bytes += r.row_bytes * rows;
+    }
+    return bytes >= kPipeMinBytes;
+}
+
+int run_row_blocks(long long rows, long long block_rows, const std::vector<MemArg*>& whole, const std::vector<RowArg>& in,
+                   const RowArg& out, const std::function<int(long long, long long, cudaStream_t)>& launch) {
+    Pipe* p = nullptr;
+    int rc = get_pipe(&p);
+    if (rc != KG_OK) return rc;
+    const long long blocks = (rows + block_rows - 1) / block_rows;
+    if (blocks > kPipeMaxChunks) return fail(KG_ERR_UNSUPPORTED, "%lld row blocks exceed the pipeline's %d", blocks, kPipeMaxChunks);
+    for (MemArg* m : whole)
+        if (m->data != nullptr && m->host) KG_CUDA_TRY(cudaMemcpyAsync(m->dev, m->data, m->bytes, cudaMemcpyHostToDevice, p->up));
+    KG_CUDA_TRY(cudaEventRecord(p->operands, p->up));
+    KG_CUDA_TRY(cudaStreamWaitEvent(p->compute, p->operands, 0));
+    for (long long c = 0; c < blocks && rc == KG_OK; ++c) {
+        const long long r0 = c * block_rows, r1 = (c + 1) * block_rows < rows ? (c + 1) * block_rows : rows;
+        for (const RowArg& r : in) {
+            const size_t off = static_cast<size_t>(r0) * r.row_bytes;
+            KG_CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(r.arg->dev) + off, static_cast<const char*>(r.arg->data) + off,
+                                        static_cast<size_t>(r1 - r0) * r.row_bytes, cudaMemcpyHostToDevice, p->up));
+        }
+        KG_CUDA_TRY(cudaEventRecord(p->uploaded[c], p->up));
+        KG_CUDA_TRY(cudaStreamWaitEvent(p->compute, p->uploaded[c], 0));
+        rc = launch(r0, r1, p->compute);
+        if (rc != KG_OK) break;
+        KG_CUDA_TRY(cudaEventRecord(p->computed[c], p->compute));
+        KG_CUDA_TRY(cudaStreamWaitEvent(p->down, p->computed[c], 0));
+        const size_t off = static_cast<size_t>(r0) * out.row_bytes;
+        KG_CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(out.arg->data) + off, static_cast<const char*>(out.arg->dev) + off,
+                                    static_cast<size_t>(r1 - r0) * out.row_bytes, cudaMemcpyDeviceToHost, p->down));
+    }
+    KG_CUDA_TRY(cudaStreamSynchronize(p->up));
+    KG_CUDA_TRY(cudaStreamSynchronize(p->compute));
+    KG_CUDA_TRY(cudaStreamSynchronize(p->down));
+    if (rc != KG_OK) return rc;
+    MemArg done = *out.arg;
+    done.host = false;  // already downloaded; finish_call only checks the device status word
+    return finish_call(KG_OK, &done, p->down);
+}
+
+// Uploads the staged host inputs. all[0] is the kernel's output, which every kernel here overwrites
+// completely (matmul, conv2d and attention write each output element exactly once), so it is not
+// uploaded.
+int upload_all_but_out(std::vector<MemArg*>& all, cudaStream_t stream) {
+    for (size_t i = 1; i < all.size(); ++i)
+        if (all[i]->data != nullptr && all[i]->host)
+            KG_CUDA_TRY(cudaMemcpyAsync(all[i]->dev, all[i]->data, all[i]->bytes, cudaMemcpyHostToDevice, stream));
     return KG_OK;
 }
 
@@ -514,7 +617,19 @@ int kg_sm100_matmul_entry(const KgArgSlot* slots, unsigned long long n) {
     std::lock_guard<std::mutex> call_lock(g_call_mu);
     cudaStream_t stream = 0;
     std::vector<MemArg*> all = {&out, &lhs, &rhs, &bias};
-    if ((rc = stage_in(all, stream))) return rc;
+    if ((rc = stage_alloc(all))) return rc;
+    const size_t esz = lhs.dtype == KG_DTYPE_BF16 ? 2 : 4;
+    const std::vector<RowArg> in = {{&lhs, static_cast<size_t>(K) * esz}};
+    const RowArg out_rows = {&out, static_cast<size_t>(W) * 4};
+    if (H >= 2 * kPipeRowBlock && pipeline_worth_it(in, out_rows, H)) {
+        long long block = (H + 7) / 8;
+        block = (block + kPipeRowBlock - 1) / kPipeRowBlock * kPipeRowBlock;
+        return run_row_blocks(H, block, {&rhs, &bias}, in, out_rows, [&](long long r0, long long r1, cudaStream_t s) {
+            return matmul_impl(static_cast<float*>(out.dev) + static_cast<size_t>(r0) * W, static_cast<const char*>(lhs.dev) + r0 * in[0].row_bytes,
+                               rhs.dev, lhs.dtype, static_cast<const float*>(bias.dev), r1 - r0, K, W, s);
+        });
+    }
+    if ((rc = upload_all_but_out(all, stream))) return rc;
     rc = matmul_impl(static_cast<float*>(out.dev), lhs.dev, rhs.dev, lhs.dtype, static_cast<const float*>(bias.dev), H, K, W, stream);
     return finish_call(rc, &out, stream);
 }
@@ -548,7 +663,20 @@ int kg_sm100_conv2d_entry(const KgArgSlot* slots, unsigned long long n) {
     std::lock_guard<std::mutex> call_lock(g_call_mu);
     cudaStream_t stream = 0;
     std::vector<MemArg*> all = {&out, &input, &weight, &bias};
-    if ((rc = stage_in(all, stream))) return rc;
+    if ((rc = stage_alloc(all))) return rc;
+    const size_t esz = input.dtype == KG_DTYPE_BF16 ? 2 : 4;
+    const std::vector<RowArg> in = {{&input, static_cast<size_t>(s.C) * s.XH * s.XW * esz}};
+    const RowArg out_rows = {&out, static_cast<size_t>(s.F) * s.HO * s.WO * 4};
+    if (pipeline_worth_it(in, out_rows, s.B)) {
+        return run_row_blocks(s.B, (s.B + 7) / 8, {&weight, &bias}, in, out_rows, [&](long long b0, long long b1, cudaStream_t st) {
+            kg::Conv2dShape part = s;
+            part.B = static_cast<int>(b1 - b0);
+            return conv2d_impl(reinterpret_cast<float*>(static_cast<char*>(out.dev) + b0 * out_rows.row_bytes),
+                               static_cast<const char*>(input.dev) + b0 * in[0].row_bytes, weight.dev, input.dtype,
+                               static_cast<const float*>(bias.dev), part, st);
+        });
+    }
+    if ((rc = upload_all_but_out(all, stream))) return rc;
     rc = conv2d_impl(static_cast<float*>(out.dev), input.dev, weight.dev, input.dtype, static_cast<const float*>(bias.dev), s, stream);
     return finish_call(rc, &out, stream);
 }
@@ -583,7 +711,20 @@ int kg_sm100_flash_attention_entry(const KgArgSlot* slots, unsigned long long n)
     std::lock_guard<std::mutex> call_lock(g_call_mu);
     cudaStream_t stream = 0;
     std::vector<MemArg*> all = {&out, &q, &k, &v};
-    if ((rc = stage_in(all, stream))) return rc;
+    if ((rc = stage_alloc(all))) return rc;
+    const long long BH = out.shape[0] * out.shape[1], S = out.shape[2], D = out.shape[3];
+    const size_t plane = static_cast<size_t>(S) * D * (q.dtype == KG_DTYPE_BF16 ? 2 : 4);  // one (b, h)
+    const std::vector<RowArg> in = {{&q, plane}, {&k, plane}, {&v, plane}};
+    const RowArg out_rows = {&out, plane};
+    if (pipeline_worth_it(in, out_rows, BH)) {
+        return run_row_blocks(BH, (BH + 7) / 8, {}, in, out_rows, [&](long long h0, long long h1, cudaStream_t st) {
+            const size_t off = static_cast<size_t>(h0) * plane;
+            return flash_attention_impl(static_cast<char*>(out.dev) + off, static_cast<const char*>(q.dev) + off,
+                                        static_cast<const char*>(k.dev) + off, static_cast<const char*>(v.dev) + off, q.dtype, 1, h1 - h0, S, D,
+                                        scale, causal, st);
+        });
+    }
+    if ((rc = upload_all_but_out(all, stream))) return rc;
     rc = flash_attention_impl(out.dev, q.dev, k.dev, v.dev, q.dtype, out.shape[0], out.shape[1], out.shape[2], out.shape[3], scale, causal,
                               stream);
     return finish_call(rc, &out, stream);

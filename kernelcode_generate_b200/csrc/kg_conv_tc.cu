@@ -302,80 +302,113 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
 }
 
-// NCHW (C channels) -> padded NHWC [B, XHp, XWp, Cp]: zero border and zero channels C..Cp.
-// Block = one padded row (x = b * XHp + hp) x 64 channels (y); 256 threads. Source pixels go in
-// chunks of 64 through a [pixel][channel] shared tile: each thread loads 8 consecutive pixels of
-// one channel (16 bytes when XW % 8 == 0) and stores 8 consecutive channels of one pixel (16 bytes),
-// so both sides move whole 128-byte lines. Border rows and columns are stored as zeros.
-// The tile's 8-channel groups are XOR-swizzled by the pixel's group of 8 so that the transposing
-// 2-byte stores of one warp land in distinct banks; each group stays 16 contiguous bytes.
-constexpr int RP_PIX = 64, RP_CH = 64;
+// One launch repacks both operands.
+//  * Input blocks (x < x_blocks): NCHW (C channels) -> padded NHWC [B, XHp, XWp, Cp], zero border
+//    and zero channels C..Cp. A block covers RP_ROWS padded rows of one image x 64 channels (y);
+//    256 threads. Source pixels go in chunks of 64 through a [row][pixel][channel] shared tile:
+//    each thread first issues all of its loads (RP_ROWS * 2 runs of 8 pixels of one channel, 16
+//    bytes each when XW % 8 == 0), then stores 8 consecutive channels of one pixel (16 bytes), so
+//    both sides move whole 128-byte lines with several loads in flight per thread. The tile's
+//    8-channel groups are XOR-swizzled by the pixel's group of 8 so that the transposing 2-byte
+//    stores of one warp land in distinct banks; each group stays 16 contiguous bytes.
+//  * Weight blocks (x >= x_blocks, y == 0): OIHW -> [F, KH*KW, Cp], zero in the channel padding;
+//    one thread per (f, c) reads the taps of weight[f, c] (contiguous) and writes one element per
+//    tap, neighbouring threads writing neighbouring c.
+constexpr int RP_PIX = 64, RP_CH = 64, RP_ROWS = 2;
+constexpr int RP_TASKS = RP_ROWS * RP_CH * (RP_PIX / 8) / 256;  // 8-pixel loads per thread per chunk
 __device__ __forceinline__ int rp_col(int px, int c) { return c ^ (((px >> 3) & 7) << 3); }
 
-__global__ void __launch_bounds__(256) nchw_to_padded_nhwc_kernel(__nv_bfloat16* __restrict__ dst, const __nv_bfloat16* __restrict__ src,
-                                                                  ConvTcShape s, int vec_ok) {
-    __shared__ __align__(16) __nv_bfloat16 tile[RP_PIX][RP_CH];
-    const int xhp = s.XH + s.pt + s.pb;
-    const int xwp = s.XW + s.pl + s.pr;
-    const int plane = static_cast<int>(blockIdx.x);
-    const int hp = plane % xhp;
-    const int b = plane / xhp;
-    const int c0 = static_cast<int>(blockIdx.y) * RP_CH;
-    const int nvec = min(RP_CH, s.Cp - c0) / 8;  // 16-byte channel groups this block writes
-    const int h = hp - s.pt;
-    __nv_bfloat16* row = dst + static_cast<size_t>(plane) * xwp * s.Cp + c0;
-    const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
-    if (h < 0 || h >= s.XH) {
-        for (int i = threadIdx.x; i < xwp * nvec; i += 256) {
-            const int px = i / nvec, v = i - px * nvec;
-            *reinterpret_cast<uint4*>(row + static_cast<size_t>(px) * s.Cp + 8 * v) = zero4;
+__global__ void __launch_bounds__(256) conv_repack_kernel(__nv_bfloat16* __restrict__ x_pad, const __nv_bfloat16* __restrict__ src,
+                                                          __nv_bfloat16* __restrict__ w_ftc, const __nv_bfloat16* __restrict__ weight,
+                                                          ConvTcShape s, int vec_ok, int x_blocks) {
+    if (static_cast<int>(blockIdx.x) >= x_blocks) {
+        if (blockIdx.y != 0) return;
+        const int taps = s.KH * s.KW;
+        const long long total = static_cast<long long>(s.F) * s.Cp;
+        const long long stride = static_cast<long long>(gridDim.x - x_blocks) * blockDim.x;
+        for (long long i = (blockIdx.x - x_blocks) * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += stride) {
+            const int f = static_cast<int>(i / s.Cp);
+            const int c = static_cast<int>(i - static_cast<long long>(f) * s.Cp);
+            const __nv_bfloat16* w = weight + (static_cast<size_t>(f) * s.C + c) * taps;
+            __nv_bfloat16* d = w_ftc + static_cast<size_t>(f) * taps * s.Cp + c;
+            for (int t = 0; t < taps; ++t) d[static_cast<size_t>(t) * s.Cp] = c < s.C ? w[t] : __float2bfloat16(0.0f);
         }
         return;
     }
-    for (int i = threadIdx.x; i < (s.pl + s.pr) * nvec; i += 256) {
-        const int k = i / nvec, v = i - k * nvec;
-        const int px = k < s.pl ? k : s.XW + k;  // left border columns, then right ones
-        *reinterpret_cast<uint4*>(row + static_cast<size_t>(px) * s.Cp + 8 * v) = zero4;
-    }
-    const __nv_bfloat16* src_row = src + (static_cast<size_t>(b) * s.C * s.XH + h) * s.XW;  // channel 0 of row h
-    const size_t ch_stride = static_cast<size_t>(s.XH) * s.XW;
-    for (int w0 = 0; w0 < s.XW; w0 += RP_PIX) {
-        for (int i = threadIdx.x; i < RP_CH * (RP_PIX / 8); i += 256) {
-            const int c = i / (RP_PIX / 8), g = i - c * (RP_PIX / 8);
-            const int w = w0 + 8 * g;
-            const int ch = c0 + c;
-            __align__(16) __nv_bfloat16 vals[8];
-            if (ch < s.C && vec_ok && w + 8 <= s.XW) {
-                *reinterpret_cast<uint4*>(vals) = *reinterpret_cast<const uint4*>(src_row + ch * ch_stride + w);
-            } else {
+    __shared__ __align__(16) __nv_bfloat16 tile[RP_ROWS][RP_PIX][RP_CH];
+    const int xhp = s.XH + s.pt + s.pb;
+    const int xwp = s.XW + s.pl + s.pr;
+    const int hblocks = (xhp + RP_ROWS - 1) / RP_ROWS;
+    const int b = static_cast<int>(blockIdx.x) / hblocks;
+    const int hp0 = (static_cast<int>(blockIdx.x) - b * hblocks) * RP_ROWS;
+    const int c0 = static_cast<int>(blockIdx.y) * RP_CH;
+    const int nvec = min(RP_CH, s.Cp - c0) / 8;  // 16-byte channel groups this block writes
+    const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
+    auto row_ptr = [&](int hp) { return x_pad + (static_cast<size_t>(b) * xhp + hp) * xwp * s.Cp + c0; };
+    auto data_row = [&](int hp) { return hp < xhp && hp - s.pt >= 0 && hp - s.pt < s.XH; };
+    // border rows (all columns) and border columns of data rows
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    vals[j] = (ch < s.C && w + j < s.XW) ? src_row[ch * ch_stride + w + j] : __float2bfloat16(0.0f);
+    for (int r = 0; r < RP_ROWS; ++r) {
+        const int hp = hp0 + r;
+        if (hp >= xhp) break;
+        __nv_bfloat16* row = row_ptr(hp);
+        if (!data_row(hp)) {
+            for (int i = threadIdx.x; i < xwp * nvec; i += 256) {
+                const int px = i / nvec, v = i - px * nvec;
+                *reinterpret_cast<uint4*>(row + static_cast<size_t>(px) * s.Cp + 8 * v) = zero4;
             }
+        } else {
+            for (int i = threadIdx.x; i < (s.pl + s.pr) * nvec; i += 256) {
+                const int k = i / nvec, v = i - k * nvec;
+                const int px = k < s.pl ? k : s.XW + k;  // left border columns, then right ones
+                *reinterpret_cast<uint4*>(row + static_cast<size_t>(px) * s.Cp + 8 * v) = zero4;
+            }
+        }
+    }
+    for (int w0 = 0; w0 < s.XW; w0 += RP_PIX) {
+        uint4 vals[RP_TASKS];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) tile[8 * g + j][rp_col(8 * g + j, c)] = vals[j];
+        for (int k = 0; k < RP_TASKS; ++k) {
+            const int t = threadIdx.x + k * 256;
+            const int r = t / (RP_CH * (RP_PIX / 8));
+            const int rem = t - r * (RP_CH * (RP_PIX / 8));
+            const int c = rem / (RP_PIX / 8), g = rem - c * (RP_PIX / 8);
+            const int hp = hp0 + r, w = w0 + 8 * g, ch = c0 + c;
+            vals[k] = zero4;
+            if (data_row(hp) && ch < s.C) {
+                const __nv_bfloat16* sp = src + ((static_cast<size_t>(b) * s.C + ch) * s.XH + (hp - s.pt)) * s.XW + w;
+                if (vec_ok && w + 8 <= s.XW) {
+                    vals[k] = *reinterpret_cast<const uint4*>(sp);
+                } else {
+                    __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&vals[k]);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (w + j < s.XW) e[j] = sp[j];
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < RP_TASKS; ++k) {
+            const int t = threadIdx.x + k * 256;
+            const int r = t / (RP_CH * (RP_PIX / 8));
+            const int rem = t - r * (RP_CH * (RP_PIX / 8));
+            const int c = rem / (RP_PIX / 8), g = rem - c * (RP_PIX / 8);
+            const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&vals[k]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) tile[r][8 * g + j][rp_col(8 * g + j, c)] = e[j];
         }
         __syncthreads();
         const int npix = min(RP_PIX, s.XW - w0);
-        for (int i = threadIdx.x; i < npix * nvec; i += 256) {
-            const int px = i / nvec, v = i - px * nvec;
-            *reinterpret_cast<uint4*>(row + static_cast<size_t>(s.pl + w0 + px) * s.Cp + 8 * v) =
-                *reinterpret_cast<const uint4*>(&tile[px][rp_col(px, 8 * v)]);
+        for (int i = threadIdx.x; i < RP_ROWS * npix * nvec; i += 256) {
+            const int r = i / (npix * nvec);
+            const int rem = i - r * (npix * nvec);
+            const int px = rem / nvec, v = rem - px * nvec;
+            const int hp = hp0 + r;
+            if (!data_row(hp)) continue;
+            *reinterpret_cast<uint4*>(row_ptr(hp) + static_cast<size_t>(s.pl + w0 + px) * s.Cp + 8 * v) =
+                *reinterpret_cast<const uint4*>(&tile[r][px][rp_col(px, 8 * v)]);
         }
         __syncthreads();
-    }
-}
-
-// OIHW -> [F, KH*KW, Cp], zero in the channel padding. One thread per (f, c): it reads the taps of
-// weight[f, c] (contiguous) and writes one element per tap; neighbouring threads write neighbouring c.
-__global__ void weight_to_ftc_kernel(__nv_bfloat16* __restrict__ dst, const __nv_bfloat16* __restrict__ src, int F, int C, int Cp, int taps) {
-    const long long total = static_cast<long long>(F) * Cp;
-    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total; i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const int f = static_cast<int>(i / Cp);
-        const int c = static_cast<int>(i - static_cast<long long>(f) * Cp);
-        const __nv_bfloat16* w = src + (static_cast<size_t>(f) * C + c) * taps;
-        __nv_bfloat16* d = dst + static_cast<size_t>(f) * taps * Cp + c;
-        for (int t = 0; t < taps; ++t) d[static_cast<size_t>(t) * Cp] = c < C ? w[t] : __float2bfloat16(0.0f);
     }
 }
 
@@ -428,16 +461,13 @@ cudaError_t conv2d_tc_repack(void* scratch, const __nv_bfloat16* input, const __
                              cudaStream_t stream) {
     __nv_bfloat16* x_pad = static_cast<__nv_bfloat16*>(scratch);
     __nv_bfloat16* w_ftc = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(scratch) + conv2d_tc_weight_offset(s));
-    const long long planes = static_cast<long long>(s.B) * conv_tc_xhp(s);
-    if (planes >= (1LL << 31)) return cudaErrorInvalidValue;
-    const int vec_ok = (s.XW % 8) == 0 && (reinterpret_cast<uintptr_t>(input) & 15u) == 0;
-    dim3 tgrid(static_cast<unsigned>(planes), (s.Cp + RP_CH - 1) / RP_CH);
-    nchw_to_padded_nhwc_kernel<<<tgrid, 256, 0, stream>>>(x_pad, input, s, vec_ok);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    const long long x_blocks = static_cast<long long>(s.B) * ((conv_tc_xhp(s) + RP_ROWS - 1) / RP_ROWS);
     const long long wtotal = static_cast<long long>(s.F) * s.Cp;
-    const int blocks = static_cast<int>((wtotal + 255) / 256 < 4096 ? (wtotal + 255) / 256 : 4096);
-    weight_to_ftc_kernel<<<blocks, 256, 0, stream>>>(w_ftc, weight, s.F, s.C, s.Cp, s.KH * s.KW);
+    const long long w_blocks = (wtotal + 255) / 256 < 1024 ? (wtotal + 255) / 256 : 1024;
+    if (x_blocks + w_blocks >= (1LL << 31)) return cudaErrorInvalidValue;
+    const int vec_ok = (s.XW % 8) == 0 && (reinterpret_cast<uintptr_t>(input) & 15u) == 0;
+    dim3 grid(static_cast<unsigned>(x_blocks + w_blocks), (s.Cp + RP_CH - 1) / RP_CH);
+    conv_repack_kernel<<<grid, 256, 0, stream>>>(x_pad, input, w_ftc, weight, s, vec_ok, static_cast<int>(x_blocks));
     return cudaGetLastError();
 }
 

@@ -188,6 +188,56 @@ def test_gemm_repeatable_bitwise(cuda_device):
     assert torch.equal(o1, o2)
 
 
+@pytest.mark.parametrize("M,with_bias", [(1000, True), (2048, False)])
+def test_host_buffer_matmul_row_blocks_match_device_path(cuda_device, M, with_bias):
+    """Host buffers through the slot entry: the call uploads rhs, then overlaps per-row-block
+    uploads, GEMMs and downloads on three streams. The result must equal the one-launch result on
+    device buffers bit for bit (a partial last block when M is not a multiple of the block)."""
+    torch = _torch()
+    rng = np.random.default_rng(M)
+    K, N = 512, 384
+    a = workloads.bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
+    b = workloads.bf16_bits(rng.standard_normal((K, N), dtype=np.float32))
+    bias = rng.standard_normal(N, dtype=np.float32) if with_bias else None
+    host_out = torch.full((M, N), float("nan")).pin_memory()
+    host_a, host_b = (torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).pin_memory() for x in (a, b))
+    host_bias = torch.from_numpy(bias).pin_memory() if with_bias else None
+    kernels.matmul_inputs_dynamic_tile_dynamic_kernel(host_out, host_a, host_b, host_bias, 128, 128, 64)
+    assert runtime.last_kernel() == "gemm_bf16_tc_pair_kernel"
+    dev_out = torch.empty(M, N, device=cuda_device)
+    kernels.matmul(dev_out, _to_torch(a, cuda_device), _to_torch(b, cuda_device), None if bias is None else _to_torch(bias, cuda_device))
+    torch.cuda.synchronize()
+    assert torch.equal(host_out, dev_out.cpu())
+    expect = oracle.matmul(a, b, bias, tiles=(128, 128, 64))
+    np.testing.assert_allclose(host_out.numpy(), expect, **BF16_TOL)
+
+
+def test_host_buffer_attention_and_conv_blocks_match_device_path(cuda_device):
+    """Host buffers of 32 MiB and more run in blocks of (b, h) planes (attention) or images
+    (conv2d) on three streams; results equal the one-launch device-buffer results bit for bit."""
+    torch = _torch()
+    g = torch.Generator().manual_seed(7)
+    q, k, v = (torch.randn(2, 16, 1024, 128, generator=g).to(torch.bfloat16).pin_memory() for _ in range(3))
+    out = torch.full_like(q, float("nan")).pin_memory()
+    kernels.flash_attention_inputs_dynamic_tile_dynamic_kernel(out, q, k, v, 128, 128, 1.0 / math.sqrt(128), True)
+    assert runtime.last_kernel() == "flash_fwd_tc_kernel"
+    ref = torch.empty(q.shape, dtype=torch.bfloat16, device=cuda_device)
+    kernels.flash_attention(ref, q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), 1.0 / math.sqrt(128), True)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref.cpu())
+
+    x = (torch.rand(16, 64, 56, 56, generator=g) * 2 - 1).to(torch.bfloat16).pin_memory()
+    w = (torch.randn(160, 64, 3, 3, generator=g) / 24).to(torch.bfloat16).pin_memory()
+    bias = torch.randn(160, generator=g).pin_memory()
+    cout = torch.full((16, 160, 56, 56), float("nan")).pin_memory()
+    kernels.conv2d_inputs_dynamic_tile_dynamic_kernel(cout, x, w, bias, 1, 1, 1, 1, 1, 1, 1, 1, 8, 16, 4, 8, 9)
+    assert runtime.last_kernel() == "conv2d_tc_kernel"
+    cref = torch.empty(cout.shape, device=cuda_device)
+    kernels.conv2d(cref, x.to(cuda_device), w.to(cuda_device), bias.to(cuda_device), (1, 1), (1, 1), (1, 1, 1, 1))
+    torch.cuda.synchronize()
+    assert torch.equal(cout, cref.cpu())
+
+
 # ---------------------------------------------------------------- flash attention
 @pytest.mark.parametrize("S,D,causal", [(128, 64, False), (257, 64, True), (300, 128, True), (1024, 128, True),
                                         (384, 128, False), (65, 32, False)])

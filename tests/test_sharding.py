@@ -83,3 +83,58 @@ def test_row_and_head_sharding_need_no_exchange():
     fa_assembled = np.concatenate([p[3].reshape(-1, 40, 16) for p in sorted(pieces, key=lambda x: x[2])], axis=0)
     np.testing.assert_array_equal(fa_assembled, fa_full)
     assert slowest == 2.0 and total == 37.0
+
+
+def _gather_worker(rank, world, port, results):
+    import torch
+    import torch.distributed as dist
+
+    from kernelcode_generate_b200.sharding import gather_rows, shard_range
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(11)
+        a = rng.standard_normal((37, 24), dtype=np.float32)
+        b = rng.standard_normal((24, 19), dtype=np.float32)
+        r0, r1 = shard_range(a.shape[0], rank, world)
+        part = torch.from_numpy(oracle.matmul(np.ascontiguousarray(a[r0:r1]), b, tiles=(8, 8, 8)))
+        mm = gather_rows(part, a.shape[0])
+        q, k, v = (rng.standard_normal((2, 3, 40, 16), dtype=np.float32) for _ in range(3))
+        b0, b1 = shard_range(6, rank, world)
+        shard = lambda x: np.ascontiguousarray(x.reshape(6, 40, 16)[b0:b1]).reshape(1, b1 - b0, 40, 16)  # noqa: E731
+        fa = torch.from_numpy(oracle.flash_attention(shard(q), shard(k), shard(v), tiles=(16, 16), scale=0.25, causal=True))
+        att = gather_rows(fa.reshape(-1, 40, 16), 6)
+        bad = None
+        try:
+            gather_rows(part[:0] if r1 > r0 else part, a.shape[0])
+        except ValueError as exc:
+            bad = str(exc)
+        if rank == 0:
+            results.put((mm.numpy(), att.numpy(), bad))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_gather_rows_assembles_the_single_process_result(world):
+    """The optional output all-gather: uneven row blocks (37 rows over 2 or 3 ranks, 6 heads over
+    3) come back as the single-process result on every rank, bit for bit."""
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    mm, att, bad = results.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    rng = np.random.default_rng(11)
+    a = rng.standard_normal((37, 24), dtype=np.float32)
+    b = rng.standard_normal((24, 19), dtype=np.float32)
+    np.testing.assert_array_equal(mm, oracle.matmul(a, b, tiles=(8, 8, 8)))
+    q, k, v = (rng.standard_normal((2, 3, 40, 16), dtype=np.float32) for _ in range(3))
+    np.testing.assert_array_equal(att, oracle.flash_attention(q, k, v, tiles=(16, 16), scale=0.25, causal=True).reshape(6, 40, 16))
+    assert bad is not None and "block" in bad
