@@ -426,6 +426,26 @@ def reference_arm(args):
     return 0
 
 
+NOMINAL_TF32_TFLOPS = 1100.0  # B200 dense TF32 tensor peak, nominal (no measured figure on this pool)
+
+
+def fp32_peak_fractions(value_tflops: float, world: int, dev) -> dict:
+    """The fp32 configurations against the dense TF32 tensor peak and the FP32 CUDA-core peak
+    (2 FLOP x 128 lanes x SMs x max SM clock), both nominal; the kernels run exact FP32 FMAs on
+    CUDA cores because TF32 cannot meet rtol 1e-4 / atol 1e-5."""
+    import torch
+
+    props = torch.cuda.get_device_properties(dev)
+    try:
+        clock_mhz = float(subprocess.run(["nvidia-smi", "--query-gpu=clocks.max.sm", "--format=csv,noheader,nounits", "-i",
+                                          str(dev.index or 0)], capture_output=True, text=True, timeout=10).stdout.split()[0])
+    except Exception:  # noqa: BLE001 - nvidia-smi missing or unparsable: the B200 nominal max clock
+        clock_mhz = 1965.0
+    simt = 2 * 128 * props.multi_processor_count * clock_mhz * 1e6 / 1e12
+    return {"frac_of_tf32_peak_nominal": round(value_tflops / (NOMINAL_TF32_TFLOPS * world), 6),
+            "fp32_simt_peak_tflops_nominal": round(simt, 1), "frac_of_fp32_simt_peak": round(value_tflops / (simt * world), 4)}
+
+
 def launches_per_step(kernel: str) -> int:
     """Kernels of this library one step launches: the tensor-core conv2d runs one repack kernel
     (input and weights) before the GEMM kernel; every other path is one kernel."""
@@ -483,6 +503,8 @@ def main(argv=None):
             suite[name] = {"value": round(v2, 3), "unit": "TFLOP/s", "ms_per_step": round(ms / steps, 4), "kernel": k2,
                            "launches_per_step": launches_per_step(k2),
                            "frac_of_bf16_peak": round(v2 / (tensor_peak * world), 4), "workload": c.note}
+            if c.dtype == "f32":
+                suite[name].update(fp32_peak_fractions(v2, world, dev))
             del w2
             torch.cuda.empty_cache()
 

@@ -17,7 +17,7 @@
 // Kernel structure as the pair GEMM (kg_gemm_tc2.cu): a cluster of 2 CTAs owns a 256-pixel x PBN-filter
 // tile; each CTA loads its own 128 pixel rows of A and PBN/2 filter rows of B (no multicast), the
 // even CTA issues tcgen05.mma.cta_group::2 256xPBNx16; the accumulator is double-buffered in TMEM so
-// the epilogue of one tile overlaps the MMAs of the next; pairs walk the tiles persistently.
+// the epilogue of one tile overlaps the MMAs of the next; each pair walks a contiguous run of tiles.
 #include "kg_conv_tc.h"
 #include "kg_ptx.cuh"
 
@@ -26,7 +26,6 @@ namespace {
 
 constexpr int PBM = 256;  // pixels per pair tile (128 per CTA)
 constexpr int BK = 64;
-constexpr int GROUP_M = 8;
 constexpr int NUM_THREADS = 192;
 constexpr uint32_t A_STAGE_BYTES = 128 * BK * 2;  // 16 KiB
 constexpr uint16_t PAIR_MASK = 0x3;
@@ -62,13 +61,9 @@ constexpr size_t conv_smem_bytes() {
 }
 
 __device__ __forceinline__ void conv_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
-    const int per_group = GROUP_M * num_n;
-    const int group = tile / per_group;
-    const int first_m = group * GROUP_M;
-    const int gsize = min(num_m - first_m, GROUP_M);
-    const int in_group = tile - group * per_group;
-    mb = first_m + in_group % gsize;
-    nb = in_group / gsize;
+    (void)num_m;
+    mb = tile / num_n;
+    nb = tile - mb * num_n;
 }
 
 template <int PBN>
@@ -97,6 +92,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const int num_m = (rows + PBM - 1) / PBM;
     const int num_n = (s.F + PBN - 1) / PBN;
     const int num_tiles = num_m * num_n;
+    // Each pair takes a contiguous run of tiles (filter blocks fastest): the next tile's input rows
+    // are the rows this tile's later taps have just read, so they come from L2.
+    const int tiles_per_pair = (num_tiles + num_pairs - 1) / num_pairs;
+    const int tile_begin = min(num_tiles, pair * tiles_per_pair);
+    const int tile_end = min(num_tiles, tile_begin + tiles_per_pair);
     const int c_blocks = (s.Cp + BK - 1) / BK;
     const int num_k = s.KH * s.KW * c_blocks;
 
@@ -134,7 +134,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             int stage = 0;
             uint32_t phase = 0;
             uint32_t issued = 0;
-            for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs) {
+            for (int tile = tile_begin; tile < tile_end && !*abort; ++tile) {
                 int mb, nb;
                 conv_tile_coords(tile, num_m, num_n, mb, nb);
                 const int row0 = mb * PBM + static_cast<int>(rank) * 128;
@@ -174,7 +174,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             int stage = 0;
             uint32_t phase = 0;
             uint32_t acc = 0, acc_phase = 0;
-            for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs) {
+            for (int tile = tile_begin; tile < tile_end && !*abort; ++tile) {
                 if (!mbar_wait_cluster(&bars->tempty[acc], acc_phase ^ 1u, abort, status, kDevTimeoutMma)) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * PBN;
@@ -224,7 +224,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const size_t plane = static_cast<size_t>(s.HO) * s.WO;
         uint32_t acc = 0, acc_phase = 0, epi_phase = 0;
         bool alive = true;
-        for (int tile = pair; tile < num_tiles && alive && !*abort; tile += num_pairs) {
+        for (int tile = tile_begin; tile < tile_end && alive && !*abort; ++tile) {
             int mb, nb;
             conv_tile_coords(tile, num_m, num_n, mb, nb);
             // this lane's 4 pixels (store phase): padded pixel -> (b, ho, wo); rows outside the output are dropped
