@@ -114,7 +114,7 @@ class ExecuteRequest:
     args: tuple
     entry_point: str | None = None
     capture_function_output: bool = False
-    stream: None = None
+    stream: Any = None  # None (reference semantics: synchronous) or a CUDA stream (extension)
 
 
 @dataclass(frozen=True)
@@ -227,14 +227,14 @@ class CompiledKernel:
         self._closed[0] = True
 
     def execute(self, args: tuple | None = None, *, request: ExecuteRequest | None = None, entry_point: str | None = None,
-                capture_function_output: bool = False, stream: None = None) -> ExecuteResult:
+                capture_function_output: bool = False, stream: Any = None) -> ExecuteResult:
         if request is not None:
             args = request.args
             entry_point = request.entry_point if entry_point is None else entry_point
             capture_function_output = request.capture_function_output
             stream = request.stream
-        if stream is not None:
-            raise KernelCodeError(_STREAM_NOT_SUPPORTED, "cuda_sm100 slot entries run on the default stream and synchronise")
+        if stream is not None and not _is_cuda_stream(stream):
+            raise KernelCodeError(_STREAM_NOT_SUPPORTED, "stream must be a torch.cuda.Stream or a cudaStream_t handle (int)")
         if capture_function_output:
             raise KernelCodeError(_FUNCTION_OUTPUT_CAPTURE_NOT_SUPPORTED,
                                   "ExecuteRequest.capture_function_output is only supported for npu_demo cost summary")
@@ -253,6 +253,8 @@ class CompiledKernel:
         if len(args) not in spec.arg_count:
             raise KernelCodeError(_RUNTIME_THROW_OR_ABORT, f"{self.function} takes {spec.arg_count} args, got {len(args)}")
         slot_args = spec.expand(args) if spec.expand else args
+        if stream is not None:
+            return self._execute_on_stream(spec, slot_args, stream)
         slots, keep = marshal_slots(slot_args, spec.absent_memory_args)
         entry = _load_entry(self.soname_path, resolved)
         t0 = time.perf_counter()
@@ -263,6 +265,43 @@ class CompiledKernel:
             raise KernelCodeError(_RUNTIME_THROW_OR_ABORT, f"entry_point returned non-zero ({status}): {runtime.last_error()}")
         return ExecuteResult(ok=True, status_code=0, failure_phrase=None, compile_stdout=self.compile_stdout,
                              compile_stderr=self.compile_stderr, elapsed_ms=elapsed)
+
+
+    def _execute_on_stream(self, spec: _KernelSpec, slot_args: tuple, stream) -> ExecuteResult:
+        """Extension (the reference requires stream=None): with CUDA tensors and a CUDA stream the
+        kernel is enqueued on that stream through the typed entry and the call returns without
+        synchronising; results are the slot entry's."""
+        from . import kernels
+
+        mem = [a for a in slot_args if a is not None and not isinstance(a, (int, float, bool))]
+        if not all(getattr(a, "is_cuda", False) for a in mem):
+            raise KernelCodeError(_STREAM_NOT_SUPPORTED, "a stream needs every memory argument to be a CUDA tensor")
+        tiles = {"matmul": slot_args[4:7], "conv2d": slot_args[12:17], "flash_attention": slot_args[4:6]}[spec.kernel]
+        if any(int(t) <= 0 for t in tiles):
+            raise KernelCodeError(_RUNTIME_THROW_OR_ABORT, "entry_point returned non-zero (1): tiles must be positive")
+        t0 = time.perf_counter()
+        try:
+            if spec.kernel == "matmul":
+                out, lhs, rhs, bias = slot_args[:4]
+                kernels.matmul(out, lhs, rhs, bias, stream=stream)
+            elif spec.kernel == "conv2d":
+                out, x, w, bias, sh, sw, dh, dw, pt, pb, pl, pr = slot_args[:12]
+                kernels.conv2d(out, x, w, bias, (sh, sw), (dh, dw), (pt, pb, pl, pr), stream=stream)
+            else:
+                out, q, k, v = slot_args[:4]
+                scale = float(slot_args[6]) if len(slot_args) == 8 else 1.0
+                causal = bool(slot_args[7]) if len(slot_args) == 8 else False
+                kernels.flash_attention(out, q, k, v, scale, causal, stream=stream)
+        except runtime.KernelError as exc:
+            raise KernelCodeError(_RUNTIME_THROW_OR_ABORT, f"entry_point returned non-zero: {exc}") from exc
+        except ValueError as exc:
+            raise KernelCodeError(_RUNTIME_THROW_OR_ABORT, str(exc)) from exc
+        return ExecuteResult(ok=True, status_code=0, failure_phrase=None, compile_stdout=self.compile_stdout,
+                             compile_stderr=self.compile_stderr, elapsed_ms=(time.perf_counter() - t0) * 1e3)
+
+
+def _is_cuda_stream(stream) -> bool:
+    return (isinstance(stream, int) and not isinstance(stream, bool)) or isinstance(getattr(stream, "cuda_stream", None), int)
 
 
 _ENTRY_CACHE: dict[tuple[str, str], Any] = {}

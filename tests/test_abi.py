@@ -117,6 +117,14 @@ def test_engine_execute_failure_phrases():
     with pytest.raises(KernelCodeError) as e:
         kernel.execute(args=(), stream=object())
     assert e.value.failure_phrase == "stream_not_supported"
+    # extension: a CUDA stream is accepted only with CUDA tensors; host arrays keep the reference phrase
+    host = (np.zeros((4, 4), np.float32), np.zeros((4, 4), np.float32), np.zeros((4, 4), np.float32), None, 4, 4, 4)
+    with pytest.raises(KernelCodeError) as e:
+        kernel.execute(args=host, stream=0)
+    assert e.value.failure_phrase == "stream_not_supported"
+    with pytest.raises(KernelCodeError) as e:
+        kernel.execute(args=host, stream=True)
+    assert e.value.failure_phrase == "stream_not_supported"
     with pytest.raises(KernelCodeError) as e:
         kernel.execute(args=(), entry_point="other")
     assert e.value.failure_phrase == "symbol_resolve_failed"

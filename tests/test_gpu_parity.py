@@ -392,3 +392,38 @@ def test_bf16_conv2d_strided_uses_cuda_cores(cuda_device):
     torch.cuda.synchronize()
     assert runtime.last_kernel() == "conv2d_simt_kernel<bf16>"
     np.testing.assert_allclose(out.cpu().numpy(), expect, **BF16_TOL)
+
+
+def test_engine_execute_on_a_stream_matches_the_synchronous_entry(cuda_device):
+    """Extension of the reference's execute(): with CUDA tensors and a CUDA stream the kernels are
+    enqueued on that stream (typed entries, no synchronisation); results equal the slot entry's."""
+    torch = _torch()
+    eng = ExecutionEngine(target="cuda_sm100")
+    side = torch.cuda.Stream()
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    a = torch.randn(512, 256, device=cuda_device, generator=g).bfloat16()
+    b = torch.randn(256, 384, device=cuda_device, generator=g).bfloat16()
+    mm = eng.compile(function="matmul_inputs_dynamic_tile_dynamic_kernel")
+    ref, got = torch.empty(512, 384, device=cuda_device), torch.full((512, 384), float("nan"), device=cuda_device)
+    mm.execute(args=(ref, a, b, None, 64, 64, 64))
+    side.wait_stream(torch.cuda.current_stream())
+    mm.execute(args=(got, a, b, None, 64, 64, 64), stream=side)
+    side.synchronize()
+    assert torch.equal(ref, got)
+    q, k, v = (torch.randn(1, 2, 300, 128, device=cuda_device, generator=g).bfloat16() for _ in range(3))
+    fa = eng.compile(function="flash_attention_inputs_dynamic_tile_dynamic_kernel")
+    fref, fgot = torch.empty_like(q), torch.empty_like(q)
+    fa.execute(args=(fref, q, k, v, 64, 64, 0.125, 1))
+    side.wait_stream(torch.cuda.current_stream())
+    fa.execute(args=(fgot, q, k, v, 64, 64, 0.125, 1), stream=side.cuda_stream)
+    side.synchronize()
+    assert torch.equal(fref, fgot)
+    x = torch.randn(2, 16, 20, 20, device=cuda_device, generator=g)
+    w = torch.randn(8, 16, 3, 3, device=cuda_device, generator=g)
+    cv = eng.compile(function="conv2d_inputs_dynamic_tile_dynamic_kernel")
+    cref, cgot = torch.empty(2, 8, 20, 20, device=cuda_device), torch.empty(2, 8, 20, 20, device=cuda_device)
+    cv.execute(args=(cref, x, w, None, 1, 1, 1, 1, 1, 1, 1, 1, 8, 16, 4, 8, 9))
+    side.wait_stream(torch.cuda.current_stream())
+    cv.execute(args=(cgot, x, w, None, 1, 1, 1, 1, 1, 1, 1, 1, 8, 16, 4, 8, 9), stream=side)
+    side.synchronize()
+    assert torch.equal(cref, cgot)
