@@ -272,6 +272,20 @@ def test_bf16_flash_attention_odd_head_count(cuda_device):
     np.testing.assert_allclose(out.float().cpu().numpy(), expect, **BF16_TOL)
 
 
+def test_f32_flash_attention_cuda_cores_many_heads(cuda_device):
+    """Many heads (4 x 40 x 256 rows, causal): 640 query blocks, several CTAs per SM, fp32
+    tolerance."""
+    torch = _torch()
+    rng = np.random.default_rng(64)
+    shape = (4, 40, 256, 64)
+    q, k, v = (rng.standard_normal(shape, dtype=np.float32) for _ in range(3))
+    expect = oracle.flash_attention(q, k, v, tiles=(64, 64), scale=0.125, causal=True)
+    out = torch.full(shape, float("nan"), device=cuda_device)
+    kernels.flash_attention(out, _to_torch(q, cuda_device), _to_torch(k, cuda_device), _to_torch(v, cuda_device), 0.125, True)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out.cpu().numpy(), expect, **FP32_TOL)
+
+
 @pytest.mark.parametrize("S,D,causal", [(200, 16, False), (130, 40, True), (257, 64, True), (96, 100, False), (333, 128, True)])
 def test_f32_flash_attention_cuda_cores_vs_oracle(cuda_device, S, D, causal):
     """fp32 attention on the CUDA-core kernel, one head-dim width per case (16 columns per thread
