@@ -284,6 +284,7 @@ def gather_run(cfg, wl, world):
         return None  # replicas: every rank already holds the whole result
     stream = torch.cuda.current_stream()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gather_rows(local, total)  # warm-up: the first NCCL all-gather also sets up its channels
     barrier(world)
     start.record(stream)
     full = gather_rows(local, total)
