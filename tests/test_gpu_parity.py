@@ -176,6 +176,53 @@ def test_c4_full_size_sampled_rows(cuda_device):
     np.testing.assert_allclose(got_colsum, expect_colsum, rtol=1e-3, atol=2.0)
 
 
+@pytest.mark.parametrize("M,K,N,with_bias", [(2000, 520, 2600, True), (2048, 512, 2560, False), (2048, 128, 2560, True),
+                                             (600, 1000, 8192, True)])
+def test_bf16_gemm_pair_tiles_over_one_wave_vs_oracle(cuda_device, M, K, N, with_bias):
+    """80-96 pair tiles of 256 x 256 on 74 pairs: a second, partly idle wave, ragged M, N and K,
+    two k-blocks, three m-blocks. Whole result vs the oracle, and bitwise repeatable."""
+    torch = _torch()
+    rng = np.random.default_rng(M + K + N)
+    a = workloads.bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
+    b = workloads.bf16_bits(rng.standard_normal((K, N), dtype=np.float32))
+    bias = rng.standard_normal(N, dtype=np.float32) if with_bias else None
+    out = torch.full((M, N), float("nan"), device=cuda_device)
+    kernels.matmul(out, _to_torch(a, cuda_device), _to_torch(b, cuda_device),
+                   None if bias is None else _to_torch(bias, cuda_device))
+    torch.cuda.synchronize()
+    assert runtime.last_kernel() == "gemm_bf16_tc_pair_kernel"
+    assert runtime.device_status() == 0
+    expect = oracle.matmul(a, b, bias, tiles=(128, 256, 64))
+    np.testing.assert_allclose(out.cpu().numpy(), expect, **BF16_TOL)
+    again = torch.full_like(out, float("nan"))
+    kernels.matmul(again, _to_torch(a, cuda_device), _to_torch(b, cuda_device),
+                   None if bias is None else _to_torch(bias, cuda_device))
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)
+
+
+def test_c4_row_shard_of_eight(cuda_device):
+    """One rank's block of C4 at 8 GPUs (1024 x 8192 x 8192, 128 pair tiles on 74 pairs). Sampled
+    rows vs the oracle and the column-sum identity over all rows."""
+    torch = _torch()
+    rng = np.random.default_rng(8)
+    M, K, N = 1024, 8192, 8192
+    a_bits = workloads.bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
+    b_bits = workloads.bf16_bits(rng.standard_normal((K, N), dtype=np.float32))
+    a, b = _to_torch(a_bits, cuda_device), _to_torch(b_bits, cuda_device)
+    out = torch.empty(M, N, device=cuda_device)
+    kernels.matmul(out, a, b)
+    torch.cuda.synchronize()
+    assert runtime.last_kernel() == "gemm_bf16_tc_pair_kernel"
+    assert runtime.device_status() == 0
+    host = out.cpu().numpy()
+    for r0 in (0, 251, 700, M - 4):
+        expect = oracle.matmul(a_bits, b_bits, tiles=(128, 256, 64), rows=(r0, r0 + 4))
+        np.testing.assert_allclose(host[r0:r0 + 4], expect[r0:r0 + 4], **BF16_TOL)
+    expect_colsum = (a.double().sum(0) @ b.double()).cpu().numpy()
+    np.testing.assert_allclose(out.double().sum(0).cpu().numpy(), expect_colsum, rtol=1e-3, atol=2.0)
+
+
 def test_gemm_repeatable_bitwise(cuda_device):
     torch = _torch()
     a = torch.randn(1024, 512, device=cuda_device).bfloat16()
