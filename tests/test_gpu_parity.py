@@ -287,7 +287,8 @@ def test_host_buffer_attention_and_conv_blocks_match_device_path(cuda_device):
 
 # ---------------------------------------------------------------- flash attention
 @pytest.mark.parametrize("S,D,causal", [(128, 64, False), (257, 64, True), (300, 128, True), (1024, 128, True),
-                                        (384, 128, False), (65, 32, False)])
+                                        (384, 128, False), (65, 32, False), (64, 128, True), (129, 128, False),
+                                        (700, 128, True), (1536, 128, False)])
 def test_bf16_flash_attention_vs_oracle(cuda_device, S, D, causal):
     torch = _torch()
     rng = np.random.default_rng(S + D)
