@@ -259,6 +259,30 @@ def test_host_buffer_matmul_row_blocks_match_device_path(cuda_device, M, with_bi
     np.testing.assert_allclose(host_out.numpy(), expect, **BF16_TOL)
 
 
+@pytest.mark.parametrize("M,K,N,with_bias", [(3000, 1024, 3000, True), (4100, 2048, 1304, False)])
+def test_host_buffer_matmul_large_row_blocks_match_device_path(cuda_device, M, K, N, with_bias):
+    """Host lhs, rhs and out of 32 MiB and more, in row blocks of 512 or 768 rows with a ragged
+    last block, N not a multiple of 256; the result equals the one-launch device-buffer result
+    bit for bit."""
+    torch = _torch()
+    rng = np.random.default_rng(M + N)
+    a = workloads.bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
+    b = workloads.bf16_bits(rng.standard_normal((K, N), dtype=np.float32))
+    bias = rng.standard_normal(N, dtype=np.float32) if with_bias else None
+    host_out = torch.full((M, N), float("nan")).pin_memory()
+    host_a, host_b = (torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).pin_memory() for x in (a, b))
+    host_bias = torch.from_numpy(bias).pin_memory() if with_bias else None
+    kernels.matmul_inputs_dynamic_tile_dynamic_kernel(host_out, host_a, host_b, host_bias, 128, 128, 64)
+    dev_out = torch.empty(M, N, device=cuda_device)
+    kernels.matmul(dev_out, _to_torch(a, cuda_device), _to_torch(b, cuda_device), None if bias is None else _to_torch(bias, cuda_device))
+    torch.cuda.synchronize()
+    assert runtime.device_status() == 0
+    assert torch.equal(host_out, dev_out.cpu())
+    for r0 in (0, M // 2, M - 3):
+        expect = oracle.matmul(a, b, bias, tiles=(128, 256, 64), rows=(r0, r0 + 3))
+        np.testing.assert_allclose(host_out.numpy()[r0:r0 + 3], expect[r0:r0 + 3], **BF16_TOL)
+
+
 def test_host_buffer_attention_and_conv_blocks_match_device_path(cuda_device):
     """Host buffers of 32 MiB and more run in blocks of (b, h) planes (attention) or images
     (conv2d) on three streams; results equal the one-launch device-buffer results bit for bit."""
