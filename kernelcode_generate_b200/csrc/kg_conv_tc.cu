@@ -18,6 +18,8 @@
 // tile; each CTA loads its own 128 pixel rows of A and PBN/2 filter rows of B (no multicast), the
 // even CTA issues tcgen05.mma.cta_group::2 256xPBNx16; the accumulator is double-buffered in TMEM so
 // the epilogue of one tile overlaps the MMAs of the next; each pair walks a contiguous run of tiles.
+// Warps per CTA: 0 TMA producer, 1 MMA issuer (even CTA), 2..9 epilogue (the epilogue is as long as
+// a tile's MMAs, so it gets two warps per TMEM lane quarter).
 #include "kg_conv_tc.h"
 #include "kg_ptx.cuh"
 
@@ -26,7 +28,7 @@ namespace {
 
 constexpr int PBM = 256;  // pixels per pair tile (128 per CTA)
 constexpr int BK = 64;
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 320;
 constexpr uint32_t A_STAGE_BYTES = 128 * BK * 2;  // 16 KiB
 constexpr uint16_t PAIR_MASK = 0x3;
 
@@ -39,7 +41,7 @@ struct ConvPairCfg {
     static constexpr uint32_t IDESC = idesc_f16(PBM, PBN, true, true, false, false);
 };
 
-constexpr int EPI_THREADS = 128;
+constexpr int EPI_THREADS = 256;
 constexpr uint32_t OUT_CHUNK_BYTES = 32 * 128 * 4;  // 32 filters x 128 pixels of f32
 
 template <int STAGES>
@@ -107,7 +109,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&bars->tfull[a], 1);
-            mbar_init(&bars->tempty[a], 8);  // lane 0 of the 4 epilogue warps of both CTAs
+            mbar_init(&bars->tempty[a], 16);  // lane 0 of the 8 epilogue warps of both CTAs
         }
         mbar_init(&bars->drain, 1);
         mbar_init(&bars->epi, EPI_THREADS);
@@ -214,12 +216,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             mbar_wait_cluster(&bars->drain, 0, &keep_waiting, status, kDevTimeoutDrain);
         }
     } else {
-        // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
-        // Per 32-filter chunk: TMEM (lane = pixel) -> shared [filter][pixel] -> each warp stores 8
+        // ------------------------------------------------------------ epilogue (warps 2..9, both CTAs)
+        // Per 32-filter chunk: TMEM (lane = pixel) -> shared [filter][pixel] -> each warp stores 4
         // filter rows, a lane writing 4 consecutive pixels (one float4 when vec_ok: the padded row
-        // pitch and WO are multiples of 4, so an aligned group of 4 pixels is one output run).
+        // pitch and WO are multiples of 4, so an aligned group of 4 pixels is one output run). Two
+        // warps share each TMEM lane quarter, one per 16-filter half of the chunk.
         const int quarter = warp & 3;  // TMEM lane quarter this warp may read
-        const int ew = warp - 2;       // filter rows ew*8 .. ew*8+7 of each chunk in the store phase
+        const int half = (warp - 2) >> 2;  // columns half*16 .. half*16+15 of each chunk
+        const int ew = warp - 2;       // filter rows ew*4 .. ew*4+3 of each chunk in the store phase
         const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&bars->tempty[0]), 0), mapa_shared(smem_u32(&bars->tempty[1]), 0)};
         const size_t plane = static_cast<size_t>(s.HO) * s.WO;
         uint32_t acc = 0, acc_phase = 0, epi_phase = 0;
@@ -247,8 +251,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * PBN;
 #pragma unroll 1
             for (int c = 0; c < PBN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(t_row + c * 32, r);
+                uint32_t r[16];
+                tmem_ld_32x32b_x16(t_row + c * 32 + half * 16, r);
                 tmem_wait_ld();
                 if (c == PBN / 32 - 1) {
                     tc_fence_before();
@@ -257,7 +261,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                 }
                 float* buf = sOut + (c & 1) * (32 * 128);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) buf[j * 128 + quarter * 32 + lane] = __uint_as_float(r[j]);
+                for (int j = 0; j < 16; ++j) buf[(half * 16 + j) * 128 + quarter * 32 + lane] = __uint_as_float(r[j]);
                 mbar_arrive(&bars->epi);
                 if (!mbar_wait(&bars->epi, epi_phase, abort, status, kDevTimeoutEpilogue)) {
                     alive = false;
@@ -265,8 +269,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                 }
                 epi_phase ^= 1u;
 #pragma unroll
-                for (int jj = 0; jj < 8; ++jj) {
-                    const int j = ew * 8 + jj;
+                for (int jj = 0; jj < 4; ++jj) {
+                    const int j = ew * 4 + jj;
                     const int f = nb * PBN + c * 32 + j;
                     if (f >= s.F) break;
                     float4 v = *reinterpret_cast<const float4*>(buf + j * 128 + 4 * lane);
