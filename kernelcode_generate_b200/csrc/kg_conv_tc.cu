@@ -133,6 +133,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer (both CTAs)
         if (lane == 0) {
+            // The kernel may start while the repack that writes its operands is finishing
+            // (programmatic dependent launch); only these loads read them.
+            asm volatile("griddepcontrol.wait;" ::: "memory");
             int stage = 0;
             uint32_t phase = 0;
             uint32_t issued = 0;
@@ -327,6 +330,9 @@ __device__ __forceinline__ int rp_col(int px, int c) { return c ^ (((px >> 3) & 
 __global__ void __launch_bounds__(256, 6) conv_repack_kernel(__nv_bfloat16* __restrict__ x_pad, const __nv_bfloat16* __restrict__ src,
                                                           __nv_bfloat16* __restrict__ w_ftc, const __nv_bfloat16* __restrict__ weight,
                                                           ConvTcShape s, int vec_ok, int x_blocks) {
+    // The conv kernel launched after this one may start setting up now; it waits for this grid to
+    // complete before reading what it writes.
+    asm volatile("griddepcontrol.launch_dependents;");
     if (static_cast<int>(blockIdx.x) >= x_blocks) {
         if (blockIdx.y != 0) return;
         const int taps = s.KH * s.KW;
@@ -438,8 +444,19 @@ cudaError_t launch_pbn(const CUtensorMap& tm_x, const CUtensorMap& tm_w, float* 
     // float4 stores need 16-byte aligned output rows and 4-pixel groups that never straddle a padded row
     const int xwp = conv_tc_xwp(s);
     const int vec_ok = (s.WO % 4) == 0 && (xwp % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
-    conv2d_tc_kernel<PBN><<<2 * pairs, NUM_THREADS, smem, stream>>>(tm_x, tm_w, out, bias, s, vec_ok, status);
-    return cudaGetLastError();
+    // Programmatic dependent launch: the CTAs' setup (barriers, TMEM, descriptor prefetch) overlaps
+    // the tail of the repack before it on the stream.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(NUM_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, conv2d_tc_kernel<PBN>, tm_x, tm_w, out, bias, s, vec_ok, status);
 }
 
 }  // namespace
