@@ -121,6 +121,22 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long rows, long l
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// 2-D f32 tensor map over a contiguous [rows, cols] matrix (dims {cols, rows}), box {32, 32}, 128B
+// swizzle (a box row is 128 bytes): the GEMM epilogue's TMA stores.
+int make_tmap_out_f32(CUtensorMap* map, void* base, long long rows, long long cols) {
+    EncodeTiledFn encode = nullptr;
+    int rc = get_encode_fn(&encode);
+    if (rc != KG_OK) return rc;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estrides[2] = {1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estrides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(KG_ERR_CUDA, "cuTensorMapEncodeTiled (out) failed (%d) rows=%lld cols=%lld", static_cast<int>(r), rows, cols);
+    return KG_OK;
+}
+
 // N-d bf16 tensor map (dims innermost first, byte strides of dims 1..rank-1), 128B swizzle.
 int make_tmap_bf16(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box) {
     EncodeTiledFn encode = nullptr;
@@ -196,7 +212,11 @@ int matmul_impl(float* out, const void* lhs, const void* rhs, int in_dtype, cons
             if (rc != KG_OK) return rc;
             if (M >= 256 && N >= 256 && dev->num_sms >= 2) {
                 g_last_kernel = "gemm_bf16_tc_pair_kernel";
-                KG_CUDA_TRY(kg::gemm_bf16_tc_pair_launch(ta, tb, out, bias, (int)M, (int)N, (int)K, dev->num_sms, dev->status, stream));
+                CUtensorMap tc;
+                const bool tma_out = N % 4 == 0 && aligned16(out);
+                if (tma_out && (rc = make_tmap_out_f32(&tc, out, M, N)) != KG_OK) return rc;
+                KG_CUDA_TRY(kg::gemm_bf16_tc_pair_launch(ta, tb, out, bias, (int)M, (int)N, (int)K, dev->num_sms, dev->status, stream,
+                                                         tma_out ? &tc : nullptr));
                 return KG_OK;
             }
             g_last_kernel = "gemm_bf16_tc_kernel";

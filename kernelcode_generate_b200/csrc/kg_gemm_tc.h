@@ -13,7 +13,9 @@ cudaError_t gemm_bf16_tc_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_b
 // CTA-pair variant (kg_gemm_tc2.cu): 256x256 tiles, same tensor maps as above. Needs M, N >= 256.
 size_t gemm_bf16_tc_pair_smem_bytes();
 cudaError_t gemm_bf16_tc_pair_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_b, float* out, const float* bias, int M, int N,
-                                     int K, int num_sms, int* status, cudaStream_t stream);
+                                     int K, int num_sms, int* status, cudaStream_t stream, const CUtensorMap* tm_c = nullptr);
+// tm_c (optional): out [M,N] f32 (dims {N, M}), box {32, 32}, 128B swizzle; the epilogue then writes
+// through TMA stores. Needs N % 4 == 0 and a 16-byte aligned out.
 int gemm_bf16_tc_tile_m();
 int gemm_bf16_tc_tile_n();
 int gemm_bf16_tc_tile_k();

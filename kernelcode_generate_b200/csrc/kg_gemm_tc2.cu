@@ -41,7 +41,9 @@ struct alignas(8) PairBarriers {
     int abort;
 };
 
-constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + sizeof(PairBarriers);
+// Epilogue staging for TMA stores: per epilogue warp two [32 rows x 32 f32] buffers, 128B-swizzled.
+constexpr uint32_t OUT_BUF_BYTES = 32 * 32 * 4;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 4 * 2 * OUT_BUF_BYTES + sizeof(PairBarriers);
 
 __device__ __forceinline__ void pair_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
     const int per_group = GROUP_M * num_n;
@@ -55,12 +57,14 @@ __device__ __forceinline__ void pair_tile_coords(int tile, int num_m, int num_n,
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, float* __restrict__ out,
-                             const float* __restrict__ bias, int M, int N, int K, int vec_ok, int* status) {
+                             const float* __restrict__ bias, int M, int N, int K, int vec_ok, int* status,
+                             const __grid_constant__ CUtensorMap tm_c, int tma_store) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-    PairBarriers* bars = reinterpret_cast<PairBarriers*>(sB + STAGES * B_STAGE_BYTES);
+    uint8_t* sC = sB + STAGES * B_STAGE_BYTES;  // [4 epilogue warps][2][32 x 128 B]
+    PairBarriers* bars = reinterpret_cast<PairBarriers*>(sC + 4 * 2 * OUT_BUF_BYTES);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -184,7 +188,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+        // With tma_store each warp stages its 32 rows x 32 columns of a chunk in shared memory
+        // (128B-swizzled: 16-byte unit k of row r at unit k ^ (r % 8)) and lane 0 stores the box with
+        // one TMA store, which writes whole 128-byte rows and drops rows and columns outside the
+        // output; the two buffers alternate, the older store having finished reading before reuse.
         const int quarter = warp & 3;
+        uint8_t* c_buf = sC + (warp - 2) * 2 * OUT_BUF_BYTES;
+        uint32_t chunk_count = 0;
         const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&bars->tempty[0]), 0), mapa_shared(smem_u32(&bars->tempty[1]), 0)};
         uint32_t acc = 0, acc_phase = 0;
         for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs) {
@@ -205,6 +215,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                     if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
                 }
                 const int col0 = nb * PBN + c * 32;
+                if (tma_store) {
+                    if (bias != nullptr && vec_ok && col0 + 32 <= N) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            const float4 bv = *reinterpret_cast<const float4*>(bias + col0 + i);
+                            r[i] = __float_as_uint(__uint_as_float(r[i]) + bv.x);
+                            r[i + 1] = __float_as_uint(__uint_as_float(r[i + 1]) + bv.y);
+                            r[i + 2] = __float_as_uint(__uint_as_float(r[i + 2]) + bv.z);
+                            r[i + 3] = __float_as_uint(__uint_as_float(r[i + 3]) + bv.w);
+                        }
+                    } else if (bias != nullptr) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (col0 + i < N) r[i] = __float_as_uint(__uint_as_float(r[i]) + bias[col0 + i]);
+                    }
+                    uint8_t* buf = c_buf + (chunk_count & 1u) * OUT_BUF_BYTES;
+                    if (lane == 0) bulk_wait_read<1>();
+                    __syncwarp();
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        *reinterpret_cast<uint4*>(buf + lane * 128 + ((k ^ (lane & 7)) << 4)) =
+                            make_uint4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
+                    fence_proxy_async_shared();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&tm_c, buf, col0, mb * PBM + static_cast<int>(rank) * 128 + quarter * 32);
+                        bulk_commit();
+                    }
+                    ++chunk_count;
+                    continue;
+                }
                 if (row < M) {
                     float* dst = out + static_cast<size_t>(row) * N + col0;
                     if (vec_ok && col0 + 32 <= N) {
@@ -232,6 +273,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             acc ^= 1u;
             if (acc == 0) acc_phase ^= 1u;
         }
+        if (tma_store && lane == 0) bulk_wait_all();  // the output is written before the CTA exits
     }
 
     tc_fence_before();
@@ -248,7 +290,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 size_t gemm_bf16_tc_pair_smem_bytes() { return SMEM_BYTES; }
 
 cudaError_t gemm_bf16_tc_pair_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_b, float* out, const float* bias, int M, int N, int K,
-                                     int num_sms, int* status, cudaStream_t stream) {
+                                     int num_sms, int* status, cudaStream_t stream, const CUtensorMap* tm_c) {
     const int vec_ok = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
                        (bias == nullptr || (reinterpret_cast<uintptr_t>(bias) & 15u) == 0);
     static bool attr_set[64] = {};
@@ -263,7 +305,8 @@ cudaError_t gemm_bf16_tc_pair_launch(const CUtensorMap& tm_a, const CUtensorMap&
     const int num_tiles = ((M + PBM - 1) / PBM) * ((N + PBN - 1) / PBN);
     const int max_pairs = num_sms / 2;
     const int pairs = num_tiles < max_pairs ? num_tiles : max_pairs;
-    gemm_bf16_tc_pair_kernel<<<2 * pairs, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, out, bias, M, N, K, vec_ok, status);
+    gemm_bf16_tc_pair_kernel<<<2 * pairs, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, out, bias, M, N, K, vec_ok, status,
+                                                                             tm_c != nullptr ? *tm_c : tm_a, tm_c != nullptr ? 1 : 0);
     return cudaGetLastError();
 }
 
