@@ -72,14 +72,6 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// Of every 4 score pairs, this many take 2^x from the FMA-pipe polynomial instead of the MUFU ex2
-// unit. With D = 128 the MUFU needs as many cycles per key tile as the tile's MMAs, but the
-// polynomial's ~10 extra instructions per pair also compete for the issue slots the MMA warp
-// needs; on B200 every non-zero setting measured slower on C5 (1 of 4: -4 %, 2 of 4: -10 %).
-#ifndef KG_FA_POLY_PER4
-#define KG_FA_POLY_PER4 0
-#endif
-
 __device__ __forceinline__ float max3(float a, float b, float c) {
     float m;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
@@ -106,27 +98,6 @@ __device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
     uint64_t d;
     asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
-}
-
-// 2^x for two values on the FMA/ALU pipes (no MUFU, no conversion instructions):
-// x = n + f with n = round(x) found by adding 1.5 * 2^23 (n lands in the low mantissa bits),
-// f = x - n in [-0.5, 0.5]; 2^f by a cubic fitted here (weighted least squares iterated
-// towards minimax relative error on [-0.5, 0.5], p(0) = 1); n is added into the exponent field.
-// Checked in float32 against exp2 over [-126, 8]: max relative error 1.0e-4, well below the
-// 3.9e-3 of the bf16 rounding P goes through. Inputs below -126 are clamped (results ~1e-38).
-__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
-    const uint64_t x = pack_f32x2(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));
-    const uint64_t t = add_f32x2(x, pack_f32x2(12582912.0f, 12582912.0f));
-    const uint64_t n = add_f32x2(t, pack_f32x2(-12582912.0f, -12582912.0f));
-    const uint64_t f = fma_f32x2(n, pack_f32x2(-1.0f, -1.0f), x);
-    uint64_t p = fma_f32x2(pack_f32x2(0.05500871f, 0.05500871f), f, pack_f32x2(0.24221054f, 0.24221054f));
-    p = fma_f32x2(p, f, pack_f32x2(0.6932829f, 0.6932829f));
-    p = fma_f32x2(p, f, pack_f32x2(1.0f, 1.0f));
-    float p0, p1, t0, t1;
-    unpack_f32x2(p, p0, p1);
-    unpack_f32x2(t, t0, t1);
-    y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-    y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
@@ -403,13 +374,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint64_t x2 = fma_f32x2(pack_f32x2(sc[c * 32 + 2 * t], sc[c * 32 + 2 * t + 1]), scale2, negm2);
                     float x0, x1;
                     unpack_f32x2(x2, x0, x1);
-                    float p0, p1;
-                    if ((t & 3) < KG_FA_POLY_PER4) {
-                        exp2_poly2(x0, x1, p0, p1);
-                    } else {
-                        p0 = ex2(x0);
-                        p1 = ex2(x1);
-                    }
+                    const float p0 = ex2(x0), p1 = ex2(x1);
                     sc[c * 32 + 2 * t] = p0;
                     sc[c * 32 + 2 * t + 1] = p1;
                     pk[t] = pack_bf16(p0, p1);
