@@ -201,6 +201,28 @@ def test_bf16_gemm_pair_tiles_over_one_wave_vs_oracle(cuda_device, M, K, N, with
     assert torch.equal(out, again)
 
 
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_bf16_gemm_pair_unaligned_output_vs_oracle(cuda_device, with_bias):
+    """An output view that starts 4 bytes into its buffer: no TMA store (it needs 16-byte rows),
+    the epilogue falls back to per-element stores; same values as the oracle."""
+    torch = _torch()
+    rng = np.random.default_rng(77)
+    M, K, N = 512, 128, 520
+    a = workloads.bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
+    b = workloads.bf16_bits(rng.standard_normal((K, N), dtype=np.float32))
+    bias = rng.standard_normal(N, dtype=np.float32) if with_bias else None
+    backing = torch.full((M * N + 1,), float("nan"), device=cuda_device)
+    out = backing[1:].view(M, N)
+    assert out.data_ptr() % 16 != 0
+    kernels.matmul(out, _to_torch(a, cuda_device), _to_torch(b, cuda_device), None if bias is None else _to_torch(bias, cuda_device))
+    torch.cuda.synchronize()
+    assert runtime.last_kernel() == "gemm_bf16_tc_pair_kernel"
+    assert runtime.device_status() == 0
+    expect = oracle.matmul(a, b, bias, tiles=(128, 256, 64))
+    np.testing.assert_allclose(out.cpu().numpy(), expect, **BF16_TOL)
+    assert math.isnan(backing[0].item())  # nothing written before the view
+
+
 def test_c4_row_shard_of_eight(cuda_device):
     """One rank's block of C4 at 8 GPUs (1024 x 8192 x 8192, 128 pair tiles on 74 pairs). Sampled
     rows vs the oracle and the column-sum identity over all rows."""
