@@ -211,12 +211,13 @@ int matmul_impl(float* out, const void* lhs, const void* rhs, int in_dtype, cons
             rc = make_tmap_2d_bf16(&tb, rhs, K, N, 64, 64);
             if (rc != KG_OK) return rc;
             if (M >= 256 && N >= 256 && dev->num_sms >= 2) {
-                g_last_kernel = "gemm_bf16_tc_pair_kernel";
+                const int block_n = kg::gemm_bf16_tc_pair_block_n((int)M, (int)N, dev->num_sms);
+                g_last_kernel = block_n == 512 ? "gemm_bf16_tc_pair_kernel<512>" : "gemm_bf16_tc_pair_kernel<256>";
                 CUtensorMap tc;
                 const bool tma_out = N % 4 == 0 && aligned16(out);
                 if (tma_out && (rc = make_tmap_out_f32(&tc, out, M, N)) != KG_OK) return rc;
                 KG_CUDA_TRY(kg::gemm_bf16_tc_pair_launch(ta, tb, out, bias, (int)M, (int)N, (int)K, dev->num_sms, dev->status, stream,
-                                                         tma_out ? &tc : nullptr));
+                                                         tma_out ? &tc : nullptr, block_n));
                 return KG_OK;
             }
             g_last_kernel = "gemm_bf16_tc_kernel";

@@ -1,4 +1,4 @@
-// bf16 x bf16 -> f32 GEMM on CTA pairs (tcgen05.mma.cta_group::2): 256 x 256 output tiles.
+// bf16 x bf16 -> f32 GEMM on CTA pairs (tcgen05.mma.cta_group::2): 256 x 256 or 256 x 512 output tiles.
 //
 // Same contract as kg_gemm_tc.cu (the reference matmul loop nest,
 // kernel/matmul/inputs_dynamic_tile_dynamic.py:84-113): out[M,N] = lhs[M,K] . rhs[K,N] (+ bias[N]).
@@ -12,6 +12,11 @@
 //   warp 1      (even CTA) MMA issuer: 4 x tcgen05.mma.cta_group::2 256x256x16 per stage, commits
 //               multicast to both CTAs' stage-release and accumulator-ready barriers.
 //   warps 2..5  epilogue of this CTA's 128 rows; releases the accumulator on the even CTA.
+// The 256 x 512 tile (two 256-column halves, 4-stage ring of 48 KB) issues two N=256 MMAs per
+// k-slice into one 512-column TMEM accumulator: 48 KB of A and B per CTA per k-step feed twice the
+// MMA work of the 256 x 256 tile's 32 KB. A quarter less L2 -> SM and DRAM traffic draws less
+// power, so under the 1 kW cap the SMs hold a higher clock; the price is a single accumulator, so
+// each tile's epilogue is not overlapped with MMAs. gemm_bf16_tc_pair_block_n picks the width.
 #include "kg_gemm_tc.h"
 #include "kg_ptx.cuh"
 
@@ -19,21 +24,30 @@ namespace kg {
 namespace {
 
 constexpr int PBM = 256;  // pair tile rows (128 per CTA)
-constexpr int PBN = 256;  // pair tile columns (128 of B per CTA)
 constexpr int BK = 64;
-constexpr int STAGES = 6;
+constexpr int MAX_STAGES = 6;
 constexpr int GROUP_M = 8;
 constexpr int NUM_THREADS = 192;
 constexpr uint32_t A_STAGE_BYTES = 128 * BK * 2;  // 16 KiB
-constexpr uint32_t B_STAGE_BYTES = BK * 128 * 2;  // 16 KiB (this CTA's half of B)
 constexpr uint32_t B_BOX_BYTES = BK * 64 * 2;     // one 64(N) x 64(K) box
-constexpr uint32_t TMEM_COLS = 2 * PBN;
-constexpr uint32_t IDESC = idesc_f16(PBM, PBN, true, true, false, true);
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t IDESC = idesc_f16(PBM, 256, true, true, false, true);  // one 256 x 256 x 16 MMA
 constexpr uint16_t PAIR_MASK = 0x3;
 
+// Pair tile of 256 x PBN (PBN = 256 or 512) as PBN / 256 halves of 256 columns. Per CTA and k-step:
+// A 128 x 64 and B 64 x (128 per half).
+template <int PBN>
+struct PairCfg {
+    static constexpr int HALVES = PBN / 256;
+    static constexpr int STAGES = HALVES == 1 ? 6 : 4;
+    static constexpr int NACC = HALVES == 1 ? 2 : 1;  // TMEM accumulators of PBN columns
+    static constexpr uint32_t B_STAGE_BYTES = HALVES * 2 * B_BOX_BYTES;
+    static_assert((PBN == 256 || PBN == 512) && STAGES <= MAX_STAGES && NACC * PBN <= static_cast<int>(TMEM_COLS), "pair tile");
+};
+
 struct alignas(8) PairBarriers {
-    uint64_t full[STAGES];
-    uint64_t empty[STAGES];
+    uint64_t full[MAX_STAGES];
+    uint64_t empty[MAX_STAGES];
     uint64_t tfull[2];
     uint64_t tempty[2];
     uint64_t drain;
@@ -43,7 +57,10 @@ struct alignas(8) PairBarriers {
 
 // Epilogue staging for TMA stores: per epilogue warp two [32 rows x 32 f32] buffers, 128B-swizzled.
 constexpr uint32_t OUT_BUF_BYTES = 32 * 32 * 4;
-constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 4 * 2 * OUT_BUF_BYTES + sizeof(PairBarriers);
+template <int PBN>
+constexpr size_t pair_smem_bytes() {
+    return 1024 + PairCfg<PBN>::STAGES * (A_STAGE_BYTES + PairCfg<PBN>::B_STAGE_BYTES) + 4 * 2 * OUT_BUF_BYTES + sizeof(PairBarriers);
+}
 
 __device__ __forceinline__ void pair_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
     const int per_group = GROUP_M * num_n;
@@ -55,10 +72,15 @@ __device__ __forceinline__ void pair_tile_coords(int tile, int num_m, int num_n,
     nb = in_group / gsize;
 }
 
+template <int PBN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_bf16_tc_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, float* __restrict__ out,
                              const float* __restrict__ bias, int M, int N, int K, int vec_ok, int* status,
                              const __grid_constant__ CUtensorMap tm_c, int tma_store) {
+    constexpr int HALVES = PairCfg<PBN>::HALVES;
+    constexpr int STAGES = PairCfg<PBN>::STAGES;
+    constexpr int NACC = PairCfg<PBN>::NACC;
+    constexpr uint32_t B_STAGE_BYTES = PairCfg<PBN>::B_STAGE_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
@@ -120,8 +142,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                     tma_load_2d_pair(sA + stage * A_STAGE_BYTES, &tm_a, leader_full, kb * BK, mb * PBM + static_cast<int>(rank) * 128);
                     uint8_t* b_dst = sB + stage * B_STAGE_BYTES;
 #pragma unroll
-                    for (int j = 0; j < 2; ++j)
-                        tma_load_2d_pair(b_dst + j * B_BOX_BYTES, &tm_b, leader_full, nb * PBN + static_cast<int>(rank) * 128 + j * 64, kb * BK);
+                    for (int j = 0; j < 2 * HALVES; ++j)  // box j: half j / 2, this CTA's 128 columns of it
+                        tma_load_2d_pair(b_dst + j * B_BOX_BYTES, &tm_b, leader_full,
+                                         nb * PBN + (j >> 1) * 256 + static_cast<int>(rank) * 128 + (j & 1) * 64, kb * BK);
                     ++issued;
                     if (++stage == STAGES) {
                         stage = 0;
@@ -150,7 +173,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
             for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs) {
                 if (!mbar_wait_cluster(&bars->tempty[acc], acc_phase ^ 1u, abort, status, kDevTimeoutMma)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + acc * PBN;
+                const uint32_t d_tmem = tmem_base + acc * PBN;  // half h at d_tmem + 256 h
                 bool ok = true;
                 for (int kb = 0; kb < num_kb; ++kb) {
                     if (!mbar_wait_cluster(&bars->full[stage], phase, abort, status, kDevTimeoutMma)) {
@@ -164,8 +187,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                         for (int kk = 0; kk < BK / 16; ++kk) {
                             const uint64_t a_desc = smem_desc_sw128(a_base + kk * 32, 16, 1024);
-                            const uint64_t b_desc = smem_desc_sw128(b_base + kk * 2048, B_BOX_BYTES, 1024);
-                            umma_f16_pair(d_tmem, a_desc, b_desc, IDESC, (kb | kk) != 0 ? 1u : 0u);
+#pragma unroll
+                            for (int h = 0; h < HALVES; ++h) {
+                                const uint64_t b_desc = smem_desc_sw128(b_base + h * 2 * B_BOX_BYTES + kk * 2048, B_BOX_BYTES, 1024);
+                                umma_f16_pair(d_tmem + h * 256, a_desc, b_desc, IDESC, (kb | kk) != 0 ? 1u : 0u);
+                            }
                         }
                         umma_commit_pair_multicast(&bars->empty[stage], PAIR_MASK);
                     }
@@ -178,8 +204,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                 if (!ok) break;
                 if (lane == 0) umma_commit_pair_multicast(&bars->tfull[acc], PAIR_MASK);
                 __syncwarp();
-                acc ^= 1u;
-                if (acc == 0) acc_phase ^= 1u;
+                if (++acc == NACC) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
             }
             if (lane == 0) umma_commit_pair(&bars->drain);
             __syncwarp();
@@ -270,8 +298,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                     }
                 }
             }
-            acc ^= 1u;
-            if (acc == 0) acc_phase ^= 1u;
+            if (++acc == NACC) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
         }
         if (tma_store && lane == 0) bulk_wait_all();  // the output is written before the CTA exits
     }
@@ -287,10 +317,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 
 }  // namespace
 
-size_t gemm_bf16_tc_pair_smem_bytes() { return SMEM_BYTES; }
+size_t gemm_bf16_tc_pair_smem_bytes() { return pair_smem_bytes<256>(); }
 
-cudaError_t gemm_bf16_tc_pair_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_b, float* out, const float* bias, int M, int N, int K,
-                                     int num_sms, int* status, cudaStream_t stream, const CUtensorMap* tm_c) {
+// 512 unless it costs more tile-columns on the busiest pair (waves x tile width) than 256: ragged
+// N (520 columns: two 512 tiles vs three 256) and grids under one wave of 256 tiles keep 256.
+int gemm_bf16_tc_pair_block_n(int M, int N, int num_sms) {
+    const long long pairs = num_sms / 2 > 0 ? num_sms / 2 : 1;
+    const long long num_m = (M + PBM - 1) / PBM;
+    auto cost = [&](long long pbn) {
+        const long long tiles = num_m * ((N + pbn - 1) / pbn);
+        return ((tiles + pairs - 1) / pairs) * pbn;
+    };
+    return cost(512) <= cost(256) ? 512 : 256;
+}
+
+template <int PBN>
+static cudaError_t launch_pbn(const CUtensorMap& tm_a, const CUtensorMap& tm_b, float* out, const float* bias, int M, int N, int K,
+                                 int num_sms, int* status, cudaStream_t stream, const CUtensorMap* tm_c) {
+    constexpr size_t SMEM_BYTES = pair_smem_bytes<PBN>();
+    static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
     const int vec_ok = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
                        (bias == nullptr || (reinterpret_cast<uintptr_t>(bias) & 15u) == 0);
     static bool attr_set[64] = {};
@@ -298,16 +343,23 @@ cudaError_t gemm_bf16_tc_pair_launch(const CUtensorMap& tm_a, const CUtensorMap&
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+        e = cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<PBN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
         if (e != cudaSuccess) return e;
         if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
     const int num_tiles = ((M + PBM - 1) / PBM) * ((N + PBN - 1) / PBN);
     const int max_pairs = num_sms / 2;
     const int pairs = num_tiles < max_pairs ? num_tiles : max_pairs;
-    gemm_bf16_tc_pair_kernel<<<2 * pairs, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, out, bias, M, N, K, vec_ok, status,
-                                                                             tm_c != nullptr ? *tm_c : tm_a, tm_c != nullptr ? 1 : 0);
+    gemm_bf16_tc_pair_kernel<PBN><<<2 * pairs, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, out, bias, M, N, K, vec_ok, status,
+                                                                                  tm_c != nullptr ? *tm_c : tm_a, tm_c != nullptr ? 1 : 0);
     return cudaGetLastError();
+}
+
+cudaError_t gemm_bf16_tc_pair_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_b, float* out, const float* bias, int M, int N, int K,
+                                     int num_sms, int* status, cudaStream_t stream, const CUtensorMap* tm_c, int block_n) {
+    if (block_n == 256) return launch_pbn<256>(tm_a, tm_b, out, bias, M, N, K, num_sms, status, stream, tm_c);
+    if (block_n == 512) return launch_pbn<512>(tm_a, tm_b, out, bias, M, N, K, num_sms, status, stream, tm_c);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace kg

@@ -138,7 +138,7 @@ def test_bf16_gemm_picks_tensor_cores_and_simt_for_unaligned(cuda_device):
     a = torch.randn(256, 256, device=cuda_device).bfloat16()
     out = torch.empty(256, 256, device=cuda_device)
     kernels.matmul(out, a, a)
-    assert runtime.last_kernel() == "gemm_bf16_tc_pair_kernel"  # M, N >= 256: CTA-pair tiles
+    assert runtime.last_kernel().startswith("gemm_bf16_tc_pair_kernel")  # M, N >= 256: CTA-pair tiles
     small = torch.randn(128, 256, device=cuda_device).bfloat16()
     out_small = torch.empty(128, 256, device=cuda_device)
     kernels.matmul(out_small, small, a)
@@ -163,6 +163,7 @@ def test_c4_full_size_sampled_rows(cuda_device):
     out = torch.empty(M, cfg.shape["N"], device=cuda_device)
     kernels.matmul(out, a, b)
     torch.cuda.synchronize()
+    assert runtime.last_kernel() == "gemm_bf16_tc_pair_kernel<512>"  # 512 tiles of 256 x 512: 6.9 waves
     assert runtime.device_status() == 0
     host = out.cpu().numpy()
     for r0 in (0, 127, 4095, 8191 - 3):
@@ -176,11 +177,18 @@ def test_c4_full_size_sampled_rows(cuda_device):
     np.testing.assert_allclose(got_colsum, expect_colsum, rtol=1e-3, atol=2.0)
 
 
-@pytest.mark.parametrize("M,K,N,with_bias", [(2000, 520, 2600, True), (2048, 512, 2560, False), (2048, 128, 2560, True),
-                                             (600, 1000, 8192, True)])
-def test_bf16_gemm_pair_tiles_over_one_wave_vs_oracle(cuda_device, M, K, N, with_bias):
-    """80-96 pair tiles of 256 x 256 on 74 pairs: a second, partly idle wave, ragged M, N and K,
-    two k-blocks, three m-blocks. Whole result vs the oracle, and bitwise repeatable."""
+PAIR_256 = "gemm_bf16_tc_pair_kernel<256>"
+PAIR_512 = "gemm_bf16_tc_pair_kernel<512>"
+
+
+@pytest.mark.parametrize("M,K,N,with_bias,kernel", [(2000, 520, 2600, True, PAIR_512), (2048, 512, 2560, False, PAIR_512),
+                                                    (2048, 128, 2560, True, PAIR_512), (600, 1000, 8192, True, PAIR_512),
+                                                    (12600, 136, 696, True, PAIR_256), (18900, 72, 1000, False, PAIR_512)])
+def test_bf16_gemm_pair_tiles_over_one_wave_vs_oracle(cuda_device, M, K, N, with_bias, kernel):
+    """Grids that need more than one wave of 256 x 256 pair tiles on 74 pairs (80-96 tiles, or one
+    wave of 40-48 256 x 512 tiles), three waves of 256 x 256 (150 tiles; 512 columns would waste a
+    third of the last n-block), two full waves of 256 x 512 (148 tiles); ragged M, N and K.
+    Whole result vs the oracle, and bitwise repeatable."""
     torch = _torch()
     rng = np.random.default_rng(M + K + N)
     a = workloads.bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
@@ -190,7 +198,7 @@ def test_bf16_gemm_pair_tiles_over_one_wave_vs_oracle(cuda_device, M, K, N, with
     kernels.matmul(out, _to_torch(a, cuda_device), _to_torch(b, cuda_device),
                    None if bias is None else _to_torch(bias, cuda_device))
     torch.cuda.synchronize()
-    assert runtime.last_kernel() == "gemm_bf16_tc_pair_kernel"
+    assert runtime.last_kernel() == kernel
     assert runtime.device_status() == 0
     expect = oracle.matmul(a, b, bias, tiles=(128, 256, 64))
     np.testing.assert_allclose(out.cpu().numpy(), expect, **BF16_TOL)
@@ -216,7 +224,7 @@ def test_bf16_gemm_pair_unaligned_output_vs_oracle(cuda_device, with_bias):
     assert out.data_ptr() % 16 != 0
     kernels.matmul(out, _to_torch(a, cuda_device), _to_torch(b, cuda_device), None if bias is None else _to_torch(bias, cuda_device))
     torch.cuda.synchronize()
-    assert runtime.last_kernel() == "gemm_bf16_tc_pair_kernel"
+    assert runtime.last_kernel().startswith("gemm_bf16_tc_pair_kernel")
     assert runtime.device_status() == 0
     expect = oracle.matmul(a, b, bias, tiles=(128, 256, 64))
     np.testing.assert_allclose(out.cpu().numpy(), expect, **BF16_TOL)
@@ -224,8 +232,8 @@ def test_bf16_gemm_pair_unaligned_output_vs_oracle(cuda_device, with_bias):
 
 
 def test_c4_row_shard_of_eight(cuda_device):
-    """One rank's block of C4 at 8 GPUs (1024 x 8192 x 8192, 128 pair tiles on 74 pairs). Sampled
-    rows vs the oracle and the column-sum identity over all rows."""
+    """One rank's block of C4 at 8 GPUs (1024 x 8192 x 8192: 64 pair tiles of 256 x 512 on 74
+    pairs). Sampled rows vs the oracle and the column-sum identity over all rows."""
     torch = _torch()
     rng = np.random.default_rng(8)
     M, K, N = 1024, 8192, 8192
@@ -235,7 +243,7 @@ def test_c4_row_shard_of_eight(cuda_device):
     out = torch.empty(M, N, device=cuda_device)
     kernels.matmul(out, a, b)
     torch.cuda.synchronize()
-    assert runtime.last_kernel() == "gemm_bf16_tc_pair_kernel"
+    assert runtime.last_kernel() == PAIR_512
     assert runtime.device_status() == 0
     host = out.cpu().numpy()
     for r0 in (0, 251, 700, M - 4):
@@ -272,7 +280,7 @@ def test_host_buffer_matmul_row_blocks_match_device_path(cuda_device, M, with_bi
     host_a, host_b = (torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).pin_memory() for x in (a, b))
     host_bias = torch.from_numpy(bias).pin_memory() if with_bias else None
     kernels.matmul_inputs_dynamic_tile_dynamic_kernel(host_out, host_a, host_b, host_bias, 128, 128, 64)
-    assert runtime.last_kernel() == "gemm_bf16_tc_pair_kernel"
+    assert runtime.last_kernel().startswith("gemm_bf16_tc_pair_kernel")
     dev_out = torch.empty(M, N, device=cuda_device)
     kernels.matmul(dev_out, _to_torch(a, cuda_device), _to_torch(b, cuda_device), None if bias is None else _to_torch(bias, cuda_device))
     torch.cuda.synchronize()
