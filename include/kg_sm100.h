@@ -92,6 +92,38 @@ KG_API int kg_sm100_conv2d_entry(const KgArgSlot* ordered_args, unsigned long lo
  * (float slot) and a causal flag (int slot). out has the dtype of q/k/v (f32 or bf16). */
 KG_API int kg_sm100_flash_attention_entry(const KgArgSlot* ordered_args, unsigned long long arg_count);
 
+/* ---------------------------------------------------------------- cost capture */
+
+/* Measured cost of one slot-entry call: the B200 counterpart of the reference's cost-mode
+ * companion `<entry>_capture(ordered_args, arg_count, output, output_capacity, output_size)`
+ * (kernel_gen/execute_engine/builtin_strategy/common.py:973-1018), which dsl_cost_run reads
+ * through ExecuteRequest.capture_function_output (kernel_gen/tools/dsl_run.py:653-690,
+ * kernel_gen/execute_engine/compiler.py:308-330). The reference's summary holds counters of its
+ * npu_demo cost model (DMA1..DMA4, MAC, VECTOR1, VECTOR2); this one holds counts and times
+ * measured on the GPU. Runs the call exactly as the slot entry does (same slots, same result in
+ * `out`), then writes into `output` a NUL-terminated JSON object with these integer keys, in
+ * this order:
+ *   FLOP       algorithmic floating-point operations: 2 per multiply-add; causal attention
+ *              counts the causal half, 2*B*H*S*S*D
+ *   MIN_BYTES  every operand read once and the output written once
+ *   H2D_BYTES  host memory the call copied to the device (0 when every operand is device memory)
+ *   D2H_BYTES  bytes the call copied back to host memory
+ *   LAUNCHES   kernels of this library launched
+ *   KERNEL_NS  device time of those launches (CUDA events around each group of launches, summed)
+ *   DEVICE_NS  device time from the call's first copy or launch to its last (CUDA events)
+ *   WALL_NS    host time of the whole call
+ * *output_size receives the text length (without the NUL). Returns 0 on success; the slot
+ * entry's error code when the call fails; KG_ERR_INVALID_ARGUMENT for a null `output` or
+ * `output_size`, a zero capacity, or a summary that does not fit (it needs at most 512 bytes);
+ * *output_size is 0 whenever the return is non-zero. The compiled-kernel shims export these as
+ * `kg_execute_entry_capture`. */
+KG_API int kg_sm100_matmul_capture(const KgArgSlot* ordered_args, unsigned long long arg_count, char* output,
+                                   unsigned long long output_capacity, unsigned long long* output_size);
+KG_API int kg_sm100_conv2d_capture(const KgArgSlot* ordered_args, unsigned long long arg_count, char* output,
+                                   unsigned long long output_capacity, unsigned long long* output_size);
+KG_API int kg_sm100_flash_attention_capture(const KgArgSlot* ordered_args, unsigned long long arg_count, char* output,
+                                            unsigned long long output_capacity, unsigned long long* output_size);
+
 /* ---------------------------------------------------------------- typed entries */
 
 /* out[M,N] (f32) = lhs[M,K] . rhs[K,N] (+ bias[N]); lhs/rhs row-major, in_dtype KG_DTYPE_F32 or

@@ -5,7 +5,7 @@
 
 Outputs (git-ignored, shipped with the working tree):
     kernelcode_generate_b200/lib/libkg_sm100.so                 all kernels + the C ABI
-    kernelcode_generate_b200/lib/libkg_sm100_<kernel>.so        `kg_execute_entry` shims
+    kernelcode_generate_b200/lib/libkg_sm100_<kernel>.so        `kg_execute_entry` (+ `_capture`) shims
 
 The CUDA runtime is linked statically so the library depends only on the driver (libcuda).
 """
@@ -88,7 +88,8 @@ def build(verbose: bool = False) -> Path:
     for name, target in SHIMS.items():
         shim = LIB_DIR / f"libkg_sm100_{name}.so"
         if _stale(shim, [shim_src, lib, INCLUDE_DIR / "kg_sm100.h"]):
-            _run(["g++", "-std=c++17", "-O2", "-fPIC", "-shared", f"-DKG_SHIM_TARGET={target}", str(shim_src),
+            capture = target.replace("_entry", "_capture")
+            _run(["g++", "-std=c++17", "-O2", "-fPIC", "-shared", f"-DKG_SHIM_TARGET={target}", f"-DKG_SHIM_CAPTURE={capture}", str(shim_src),
                   "-L", str(LIB_DIR), "-l:" + LIB_NAME, "-Wl,-rpath,$ORIGIN", "-o", str(shim)])
     if verbose:
         print(f"built {lib}")

@@ -4,6 +4,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <chrono>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -369,6 +370,58 @@ struct MemArg {
     bool host = false;          // caller passed host memory: staged through `dev`
 };
 
+// ------------------------------------------------------------------ cost capture
+// While a *_capture entry runs a slot entry on this thread, t_cost collects what the call did:
+// work counts, staged bytes, and CUDA events around its first copy or launch, its last copy, and
+// each group of kernel launches. Without a capture every hook below returns at once.
+struct CostRec {
+    unsigned long long flop = 0, min_bytes = 0, h2d = 0, d2h = 0, launches = 0;
+    std::vector<cudaEvent_t> events;                             // every event created for the call
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> launch_spans;
+    cudaEvent_t first = nullptr, last = nullptr;
+    bool event_failed = false;
+};
+thread_local CostRec* t_cost = nullptr;
+
+cudaEvent_t cost_event() {
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) {
+        t_cost->event_failed = true;
+        return nullptr;
+    }
+    t_cost->events.push_back(e);
+    return e;
+}
+
+void cost_mark_first(cudaStream_t s) {
+    if (t_cost == nullptr || t_cost->first != nullptr || t_cost->event_failed) return;
+    if ((t_cost->first = cost_event()) != nullptr && cudaEventRecord(t_cost->first, s) != cudaSuccess) t_cost->event_failed = true;
+}
+
+void cost_mark_last(cudaStream_t s) {
+    if (t_cost == nullptr || t_cost->event_failed) return;
+    if (t_cost->last == nullptr && (t_cost->last = cost_event()) == nullptr) return;
+    if (cudaEventRecord(t_cost->last, s) != cudaSuccess) t_cost->event_failed = true;
+}
+
+// Kernels one *_impl call launches: the tensor-core conv2d repacks first, everything else is one launch.
+unsigned long long launches_of(const char* kernel) { return std::strcmp(kernel, "conv2d_tc_kernel") == 0 ? 2 : 1; }
+
+// Runs one *_impl call (its kernels back to back on `s`), timed with an event pair when a cost
+// capture is active.
+int cost_timed(cudaStream_t s, const std::function<int()>& launch) {
+    if (t_cost == nullptr) return launch();
+    cudaEvent_t a = cost_event(), b = cost_event();
+    if (a != nullptr && cudaEventRecord(a, s) != cudaSuccess) t_cost->event_failed = true;
+    const int rc = launch();
+    if (b != nullptr && cudaEventRecord(b, s) != cudaSuccess) t_cost->event_failed = true;
+    if (rc == KG_OK) {
+        t_cost->launches += launches_of(g_last_kernel);
+        if (a != nullptr && b != nullptr) t_cost->launch_spans.emplace_back(a, b);
+    }
+    return rc;
+}
+
 int read_mem(const KgArgSlot* slots, unsigned long long i, const char* name, bool optional, int rank, MemArg* m) {
     const KgArgSlot& s = slots[i];
     if (s.kind != KG_SLOT_MEMORY) return fail(KG_ERR_INVALID_ARGUMENT, "slot %llu (%s): expected memory, got kind %d", i, name, s.kind);
@@ -488,6 +541,7 @@ int finish_call(int rc, MemArg* out, cudaStream_t stream) {
         return rc;
     }
     if (out->host) KG_CUDA_TRY(cudaMemcpyAsync(out->data, out->dev, out->bytes, cudaMemcpyDeviceToHost, stream));
+    cost_mark_last(stream);
     KG_CUDA_TRY(cudaStreamSynchronize(stream));
     DeviceInfo* dev = nullptr;
     rc = device_info(&dev);
@@ -531,6 +585,7 @@ int run_row_blocks(long long rows, long long block_rows, const std::vector<MemAr
     if (rc != KG_OK) return rc;
     const long long blocks = (rows + block_rows - 1) / block_rows;
     if (blocks > kPipeMaxChunks) return fail(KG_ERR_UNSUPPORTED, "%lld row blocks exceed the pipeline's %d", blocks, kPipeMaxChunks);
+    cost_mark_first(p->up);
     for (MemArg* m : whole)
         if (m->data != nullptr && m->host) KG_CUDA_TRY(cudaMemcpyAsync(m->dev, m->data, m->bytes, cudaMemcpyHostToDevice, p->up));
     KG_CUDA_TRY(cudaEventRecord(p->operands, p->up));
@@ -544,7 +599,7 @@ int run_row_blocks(long long rows, long long block_rows, const std::vector<MemAr
         }
         KG_CUDA_TRY(cudaEventRecord(p->uploaded[c], p->up));
         KG_CUDA_TRY(cudaStreamWaitEvent(p->compute, p->uploaded[c], 0));
-        rc = launch(r0, r1, p->compute);
+        rc = cost_timed(p->compute, [&] { return launch(r0, r1, p->compute); });
         if (rc != KG_OK) break;
         KG_CUDA_TRY(cudaEventRecord(p->computed[c], p->compute));
         KG_CUDA_TRY(cudaStreamWaitEvent(p->down, p->computed[c], 0));
@@ -565,10 +620,23 @@ int run_row_blocks(long long rows, long long block_rows, const std::vector<MemAr
 // completely (matmul, conv2d and attention write each output element exactly once), so it is not
 // uploaded.
 int upload_all_but_out(std::vector<MemArg*>& all, cudaStream_t stream) {
+    cost_mark_first(stream);
     for (size_t i = 1; i < all.size(); ++i)
         if (all[i]->data != nullptr && all[i]->host)
             KG_CUDA_TRY(cudaMemcpyAsync(all[i]->dev, all[i]->data, all[i]->bytes, cudaMemcpyHostToDevice, stream));
     return KG_OK;
+}
+
+// Work and staging counts of a slot-entry call, for an active cost capture. all[0] is the output.
+void cost_work(double flop, const std::vector<MemArg*>& all) {
+    if (t_cost == nullptr) return;
+    t_cost->flop = static_cast<unsigned long long>(flop);
+    for (size_t i = 0; i < all.size(); ++i) {
+        const MemArg* m = all[i];
+        if (m->data == nullptr) continue;
+        t_cost->min_bytes += m->bytes;
+        if (m->host) (i == 0 ? t_cost->d2h : t_cost->h2d) += m->bytes;
+    }
 }
 
 }  // namespace
@@ -639,6 +707,7 @@ int kg_sm100_matmul_entry(const KgArgSlot* slots, unsigned long long n) {
     cudaStream_t stream = 0;
     std::vector<MemArg*> all = {&out, &lhs, &rhs, &bias};
     if ((rc = stage_alloc(all))) return rc;
+    cost_work(2.0 * H * K * W, all);
     const size_t esz = lhs.dtype == KG_DTYPE_BF16 ? 2 : 4;
     const std::vector<RowArg> in = {{&lhs, static_cast<size_t>(K) * esz}};
     const RowArg out_rows = {&out, static_cast<size_t>(W) * 4};
@@ -651,7 +720,9 @@ int kg_sm100_matmul_entry(const KgArgSlot* slots, unsigned long long n) {
         });
     }
     if ((rc = upload_all_but_out(all, stream))) return rc;
-    rc = matmul_impl(static_cast<float*>(out.dev), lhs.dev, rhs.dev, lhs.dtype, static_cast<const float*>(bias.dev), H, K, W, stream);
+    rc = cost_timed(stream, [&] {
+        return matmul_impl(static_cast<float*>(out.dev), lhs.dev, rhs.dev, lhs.dtype, static_cast<const float*>(bias.dev), H, K, W, stream);
+    });
     return finish_call(rc, &out, stream);
 }
 
@@ -685,6 +756,7 @@ int kg_sm100_conv2d_entry(const KgArgSlot* slots, unsigned long long n) {
     cudaStream_t stream = 0;
     std::vector<MemArg*> all = {&out, &input, &weight, &bias};
     if ((rc = stage_alloc(all))) return rc;
+    cost_work(2.0 * s.B * s.F * s.HO * s.WO * s.C * s.KH * s.KW, all);
     const size_t esz = input.dtype == KG_DTYPE_BF16 ? 2 : 4;
     const std::vector<RowArg> in = {{&input, static_cast<size_t>(s.C) * s.XH * s.XW * esz}};
     const RowArg out_rows = {&out, static_cast<size_t>(s.F) * s.HO * s.WO * 4};
@@ -698,7 +770,9 @@ int kg_sm100_conv2d_entry(const KgArgSlot* slots, unsigned long long n) {
         });
     }
     if ((rc = upload_all_but_out(all, stream))) return rc;
-    rc = conv2d_impl(static_cast<float*>(out.dev), input.dev, weight.dev, input.dtype, static_cast<const float*>(bias.dev), s, stream);
+    rc = cost_timed(stream, [&] {
+        return conv2d_impl(static_cast<float*>(out.dev), input.dev, weight.dev, input.dtype, static_cast<const float*>(bias.dev), s, stream);
+    });
     return finish_call(rc, &out, stream);
 }
 
@@ -734,6 +808,7 @@ int kg_sm100_flash_attention_entry(const KgArgSlot* slots, unsigned long long n)
     std::vector<MemArg*> all = {&out, &q, &k, &v};
     if ((rc = stage_alloc(all))) return rc;
     const long long BH = out.shape[0] * out.shape[1], S = out.shape[2], D = out.shape[3];
+    cost_work((causal ? 2.0 : 4.0) * BH * S * S * D, all);  // causal: the causal-half count
     const size_t plane = static_cast<size_t>(S) * D * (q.dtype == KG_DTYPE_BF16 ? 2 : 4);  // one (b, h)
     const std::vector<RowArg> in = {{&q, plane}, {&k, plane}, {&v, plane}};
     const RowArg out_rows = {&out, plane};
@@ -746,9 +821,78 @@ int kg_sm100_flash_attention_entry(const KgArgSlot* slots, unsigned long long n)
         });
     }
     if ((rc = upload_all_but_out(all, stream))) return rc;
-    rc = flash_attention_impl(out.dev, q.dev, k.dev, v.dev, q.dtype, out.shape[0], out.shape[1], out.shape[2], out.shape[3], scale, causal,
-                              stream);
+    rc = cost_timed(stream, [&] {
+        return flash_attention_impl(out.dev, q.dev, k.dev, v.dev, q.dtype, out.shape[0], out.shape[1], out.shape[2], out.shape[3], scale,
+                                    causal, stream);
+    });
     return finish_call(rc, &out, stream);
+}
+
+}  // extern "C"
+
+namespace {
+
+// Runs `entry` with a cost recorder on this thread and writes the summary (format in kg_sm100.h).
+int capture_call(int (*entry)(const KgArgSlot*, unsigned long long), const KgArgSlot* slots, unsigned long long n, char* output,
+                 unsigned long long capacity, unsigned long long* output_size) {
+    if (output == nullptr || output_size == nullptr || capacity == 0)
+        return fail(KG_ERR_INVALID_ARGUMENT, "capture: null output buffer or size pointer, or zero capacity");
+    *output_size = 0;
+    CostRec rec;
+    t_cost = &rec;
+    const auto t0 = std::chrono::steady_clock::now();
+    int rc = entry(slots, n);
+    const auto t1 = std::chrono::steady_clock::now();
+    t_cost = nullptr;
+    // A successful entry synchronised every stream it used, so all recorded events have completed.
+    double kernel_ms = 0.0, device_ms = 0.0;
+    float ms = 0.0f;
+    cudaError_t e = cudaSuccess;
+    if (rc == KG_OK && !rec.event_failed) {
+        for (const auto& span : rec.launch_spans) {
+            if (e == cudaSuccess && (e = cudaEventElapsedTime(&ms, span.first, span.second)) == cudaSuccess) kernel_ms += ms;
+        }
+        if (e == cudaSuccess && rec.first != nullptr && rec.last != nullptr &&
+            (e = cudaEventElapsedTime(&ms, rec.first, rec.last)) == cudaSuccess)
+            device_ms = ms;
+        if (e != cudaSuccess) cudaGetLastError();  // not left behind for the next launch check
+    }
+    for (cudaEvent_t ev : rec.events) cudaEventDestroy(ev);
+    if (rc != KG_OK) return rc;
+    if (rec.event_failed) return fail(KG_ERR_CUDA, "capture: creating or recording a timing event failed");
+    if (e != cudaSuccess) return cuda_fail(e, "capture: cudaEventElapsedTime");
+    const long long wall_ns = std::chrono::duration_cast<std::chrono::nanoseconds>(t1 - t0).count();
+    char text[512];
+    const int len = std::snprintf(text, sizeof(text),
+                                  "{\"FLOP\":%llu,\"MIN_BYTES\":%llu,\"H2D_BYTES\":%llu,\"D2H_BYTES\":%llu,\"LAUNCHES\":%llu,"
+                                  "\"KERNEL_NS\":%lld,\"DEVICE_NS\":%lld,\"WALL_NS\":%lld}",
+                                  rec.flop, rec.min_bytes, rec.h2d, rec.d2h, rec.launches, std::llround(kernel_ms * 1e6),
+                                  std::llround(device_ms * 1e6), wall_ns);
+    if (len < 0 || static_cast<size_t>(len) >= sizeof(text)) return fail(KG_ERR_CUDA, "capture: summary formatting failed");
+    if (static_cast<unsigned long long>(len) >= capacity)
+        return fail(KG_ERR_INVALID_ARGUMENT, "capture: the summary needs %d bytes, output capacity is %llu", len + 1, capacity);
+    std::memcpy(output, text, static_cast<size_t>(len) + 1);
+    *output_size = static_cast<unsigned long long>(len);
+    return KG_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int kg_sm100_matmul_capture(const KgArgSlot* slots, unsigned long long n, char* output, unsigned long long capacity,
+                            unsigned long long* output_size) {
+    return capture_call(kg_sm100_matmul_entry, slots, n, output, capacity, output_size);
+}
+
+int kg_sm100_conv2d_capture(const KgArgSlot* slots, unsigned long long n, char* output, unsigned long long capacity,
+                            unsigned long long* output_size) {
+    return capture_call(kg_sm100_conv2d_entry, slots, n, output, capacity, output_size);
+}
+
+int kg_sm100_flash_attention_capture(const KgArgSlot* slots, unsigned long long n, char* output, unsigned long long capacity,
+                                     unsigned long long* output_size) {
+    return capture_call(kg_sm100_flash_attention_entry, slots, n, output, capacity, output_size);
 }
 
 }  // extern "C"

@@ -20,6 +20,10 @@ What differs, by design:
 * Memory arguments may be torch CUDA tensors (device pointers, no copies) as well as numpy
   arrays / CPU tensors (staged through device memory inside the call).
 * bf16 memory (torch.bfloat16) is accepted with dtype code 5; the reference has no bf16 code.
+* ``capture_function_output=True`` (the reference allows it only for npu_demo cost summaries,
+  compiler.py:308-330) calls the shim's ``kg_execute_entry_capture`` companion: the call runs as
+  usual and ``ExecuteResult.run_stdout`` holds its measured cost summary, a JSON object of integer
+  counts and times (keys in include/kg_sm100.h; ``cost_run.py`` reads it).
 """
 
 from __future__ import annotations
@@ -235,9 +239,9 @@ class CompiledKernel:
             stream = request.stream
         if stream is not None and not _is_cuda_stream(stream):
             raise KernelCodeError(_STREAM_NOT_SUPPORTED, "stream must be a torch.cuda.Stream or a cudaStream_t handle (int)")
-        if capture_function_output:
+        if capture_function_output and stream is not None:
             raise KernelCodeError(_FUNCTION_OUTPUT_CAPTURE_NOT_SUPPORTED,
-                                  "ExecuteRequest.capture_function_output is only supported for npu_demo cost summary")
+                                  "the cost summary capture runs the synchronous slot entry: stream must be None")
         if self._closed[0]:
             raise KernelCodeError(_RUNTIME_THROW_OR_ABORT, "compiled kernel is closed")
         if args is None:
@@ -256,6 +260,8 @@ class CompiledKernel:
         if stream is not None:
             return self._execute_on_stream(spec, slot_args, stream)
         slots, keep = marshal_slots(slot_args, spec.absent_memory_args)
+        if capture_function_output:
+            return self._execute_capture(slots, keep, len(slot_args), resolved)
         entry = _load_entry(self.soname_path, resolved)
         t0 = time.perf_counter()
         status = int(entry(slots, ctypes.c_ulonglong(len(slot_args))))
@@ -266,6 +272,25 @@ class CompiledKernel:
         return ExecuteResult(ok=True, status_code=0, failure_phrase=None, compile_stdout=self.compile_stdout,
                              compile_stderr=self.compile_stderr, elapsed_ms=elapsed)
 
+
+    def _execute_capture(self, slots, keep, arg_count: int, entry_point: str) -> ExecuteResult:
+        """Runs the call through `<entry_point>_capture` and returns its cost summary as run_stdout."""
+        try:
+            capture = _load_capture(self.soname_path, entry_point)
+        except KernelCodeError as exc:
+            raise KernelCodeError(_FUNCTION_OUTPUT_CAPTURE_NOT_SUPPORTED,
+                                  "compiled kernel does not expose function output capture companion") from exc
+        capacity = 1024
+        text = ctypes.create_string_buffer(capacity)
+        size = ctypes.c_ulonglong(0)
+        t0 = time.perf_counter()
+        status = int(capture(slots, ctypes.c_ulonglong(arg_count), text, ctypes.c_ulonglong(capacity), ctypes.byref(size)))
+        elapsed = (time.perf_counter() - t0) * 1e3
+        del keep
+        if status != 0:
+            raise KernelCodeError(_RUNTIME_THROW_OR_ABORT, f"entry_point returned non-zero ({status}): {runtime.last_error()}")
+        return ExecuteResult(ok=True, status_code=0, failure_phrase=None, compile_stdout=self.compile_stdout,
+                             compile_stderr=self.compile_stderr, run_stdout=text.raw[:size.value].decode("ascii"), elapsed_ms=elapsed)
 
     def _execute_on_stream(self, spec: _KernelSpec, slot_args: tuple, stream) -> ExecuteResult:
         """Extension (the reference requires stream=None): with CUDA tensors and a CUDA stream the
@@ -320,6 +345,22 @@ def _load_entry(soname_path: str, entry_point: str):
         except AttributeError as exc:
             raise KernelCodeError(_SYMBOL_RESOLVE_FAILED, f"entry_point '{entry_point}' is missing") from exc
         fn.argtypes = [ctypes.POINTER(runtime.KgArgSlot), ctypes.c_ulonglong]
+        fn.restype = ctypes.c_int
+        _ENTRY_CACHE[key] = fn
+    return _ENTRY_CACHE[key]
+
+
+def _load_capture(soname_path: str, entry_point: str):
+    key = (soname_path, entry_point + "_capture")
+    if key not in _ENTRY_CACHE:
+        runtime.load()
+        try:
+            lib = ctypes.CDLL(soname_path)
+            fn = getattr(lib, entry_point + "_capture")
+        except (OSError, AttributeError) as exc:
+            raise KernelCodeError(_SYMBOL_RESOLVE_FAILED, f"entry_point '{entry_point}_capture' is missing") from exc
+        fn.argtypes = [ctypes.POINTER(runtime.KgArgSlot), ctypes.c_ulonglong, ctypes.c_char_p, ctypes.c_ulonglong,
+                       ctypes.POINTER(ctypes.c_ulonglong)]
         fn.restype = ctypes.c_int
         _ENTRY_CACHE[key] = fn
     return _ENTRY_CACHE[key]

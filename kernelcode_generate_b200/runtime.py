@@ -27,6 +27,9 @@ EXPORTED_SYMBOLS = (
     "kg_sm100_matmul_entry",
     "kg_sm100_conv2d_entry",
     "kg_sm100_flash_attention_entry",
+    "kg_sm100_matmul_capture",
+    "kg_sm100_conv2d_capture",
+    "kg_sm100_flash_attention_capture",
     "kg_sm100_matmul",
     "kg_sm100_conv2d",
     "kg_sm100_flash_attention",

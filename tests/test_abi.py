@@ -51,6 +51,7 @@ def test_compiled_kernel_shims_export_kg_execute_entry():
     for path in runtime.SHIM_PATHS.values():
         lib = ctypes.CDLL(str(path))
         assert hasattr(lib, "kg_execute_entry")
+        assert hasattr(lib, "kg_execute_entry_capture")
 
 
 def test_abi_version_and_no_gpu_error_path():
@@ -136,6 +137,9 @@ def test_engine_execute_failure_phrases():
     assert e.value.failure_phrase == "runtime_throw_or_abort"
     with pytest.raises(KernelCodeError) as e:
         kernel.execute(args=(), capture_function_output=True)
+    assert e.value.failure_phrase == "runtime_throw_or_abort"  # capture is served; the argument count is checked first
+    with pytest.raises(KernelCodeError) as e:
+        kernel.execute(args=host, capture_function_output=True, stream=0)
     assert e.value.failure_phrase == "function_output_capture_not_supported"
     kernel.close()
     kernel.close()
