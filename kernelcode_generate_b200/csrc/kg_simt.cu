@@ -170,68 +170,85 @@ __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ ou
 }
 
 // ------------------------------------------------------------------ flash attention
-// One CTA = 64 query rows of one (b, h); 256 threads as 16 x 16 (ty, tx). Key/value tiles of 64
-// rows. Thread (ty, tx) owns scores rows 4ty..4ty+3 x keys 4tx..4tx+3 and output rows 4ty..4ty+3 x
-// head columns tx, tx+16, ... (DT of them, D padded to 16*DT). Q and K are staged transposed
-// ([d][row]) so each step of Q.K^T is two float4 shared loads for 16 FMAs; P goes through shared
-// memory to the P.V product. Row max / sum combine over the 16 tx threads of a row with shuffles.
-constexpr int FA_BR = 64, FA_BC = 64;
+// One CTA = 16*RA query rows of one (b, h); 256 threads as 16 x 16 (ty, tx). Key/value tiles of 64
+// rows. Thread (ty, tx) owns scores rows RA*ty..RA*ty+RA-1 x keys 4tx..4tx+3 and the same output
+// rows x head columns tx, tx+16, ... (DT of them, D padded to 16*DT). Q and K are staged transposed
+// ([d][row]) so each step of Q.K^T is one RA-wide and one float4 shared load for 4*RA FMAs; P goes
+// through shared memory to the P.V product. Row max / sum combine over the 16 tx threads of a row
+// with shuffles. RA (4, 2 or 1 rows per thread) is chosen per call so small problems still spread
+// over the SMs: every output element is computed the same way whatever RA is.
+constexpr int FA_BC = 64;
 
-template <typename T, int DT>
+template <int RA>
+__device__ __forceinline__ void load_rows(const float* p, float (&r)[RA]) {
+    if constexpr (RA == 4) {
+        const float4 t = *reinterpret_cast<const float4*>(p);
+        r[0] = t.x, r[1] = t.y, r[2] = t.z, r[3] = t.w;
+    } else if constexpr (RA == 2) {
+        const float2 t = *reinterpret_cast<const float2*>(p);
+        r[0] = t.x, r[1] = t.y;
+    } else {
+        r[0] = *p;
+    }
+}
+
+template <typename T, int DT, int RA>
 __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__ out, const T* __restrict__ q, const T* __restrict__ k,
                                                               const T* __restrict__ v, int H, int S, int D, float scale_log2, int causal) {
     constexpr int DP = 16 * DT;          // padded head dim
-    constexpr int LDT = FA_BR + 4;       // row pitch of the transposed tiles
+    constexpr int BR = 16 * RA;          // query rows per CTA
+    constexpr int LDQ = BR + 4;          // row pitch of the transposed Q tile
+    constexpr int LDK = FA_BC + 4;       // row pitch of the transposed K tile
     extern __shared__ float4 fa_smem4[];
     float* fa_smem = reinterpret_cast<float*>(fa_smem4);
-    float* sQt = fa_smem;                // [DP][LDT]
-    float* sKt = sQt + DP * LDT;         // [DP][LDT]
-    float* sV = sKt + DP * LDT;          // [FA_BC][DP + 4]
-    float* sP = sV + FA_BC * (DP + 4);   // [FA_BR][FA_BC + 4]
+    float* sQt = fa_smem;                // [DP][LDQ]
+    float* sKt = sQt + DP * LDQ;         // [DP][LDK]
+    float* sV = sKt + DP * LDK;          // [FA_BC][DP + 4]
+    float* sP = sV + FA_BC * (DP + 4);   // [BR][FA_BC + 4]
     const int bh = blockIdx.y;
-    const int m0 = blockIdx.x * FA_BR;
+    const int m0 = blockIdx.x * BR;
     const size_t base = (size_t)bh * S * D;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
 
-    for (int i = threadIdx.x; i < FA_BR * DP; i += 256) {
+    for (int i = threadIdx.x; i < BR * DP; i += 256) {
         const int r = i / DP, d = i - r * DP;
-        sQt[d * LDT + r] = (m0 + r < S && d < D) ? to_f32(q[base + (size_t)(m0 + r) * D + d]) : 0.0f;
+        sQt[d * LDQ + r] = (m0 + r < S && d < D) ? to_f32(q[base + (size_t)(m0 + r) * D + d]) : 0.0f;
     }
-    float o[4][DT];
-    float m_run[4], l_run[4];
+    float o[RA][DT];
+    float m_run[RA], l_run[RA];
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
+    for (int a = 0; a < RA; ++a) {
         m_run[a] = -INFINITY;
         l_run[a] = 0.0f;
 #pragma unroll
         for (int c = 0; c < DT; ++c) o[a][c] = 0.0f;
     }
-    const int n_end = causal ? min(S, m0 + FA_BR) : S;
+    const int n_end = causal ? min(S, m0 + BR) : S;
     for (int n0 = 0; n0 < n_end; n0 += FA_BC) {
         __syncthreads();
         for (int i = threadIdx.x; i < FA_BC * DP; i += 256) {
             const int j = i / DP, d = i - j * DP;
             const bool ok = n0 + j < S && d < D;
-            sKt[d * LDT + j] = ok ? to_f32(k[base + (size_t)(n0 + j) * D + d]) : 0.0f;
+            sKt[d * LDK + j] = ok ? to_f32(k[base + (size_t)(n0 + j) * D + d]) : 0.0f;
             sV[j * (DP + 4) + d] = ok ? to_f32(v[base + (size_t)(n0 + j) * D + d]) : 0.0f;
         }
         __syncthreads();
-        float sc[4][4] = {};
+        float sc[RA][4] = {};
 #pragma unroll 4
         for (int d = 0; d < DP; ++d) {
-            const float4 qa = *reinterpret_cast<const float4*>(sQt + d * LDT + 4 * ty);
-            const float4 kb = *reinterpret_cast<const float4*>(sKt + d * LDT + 4 * tx);
-            const float qv[4] = {qa.x, qa.y, qa.z, qa.w};
+            float qv[RA];
+            load_rows<RA>(sQt + d * LDQ + RA * ty, qv);
+            const float4 kb = *reinterpret_cast<const float4*>(sKt + d * LDK + 4 * tx);
             const float kv[4] = {kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
+            for (int a = 0; a < RA; ++a)
 #pragma unroll
                 for (int b = 0; b < 4; ++b) sc[a][b] = fmaf(qv[a], kv[b], sc[a][b]);
         }
-        float alpha[4];
+        float alpha[RA];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) {
-            const int row = m0 + 4 * ty + a;
+        for (int a = 0; a < RA; ++a) {
+            const int row = m0 + RA * ty + a;
             float mx = -INFINITY;
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
@@ -251,7 +268,7 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
             for (int b = 0; b < 4; ++b) {
                 const float p = exp2f(sc[a][b] - m_use);
                 psum += p;
-                sP[(4 * ty + a) * (FA_BC + 4) + 4 * tx + b] = p;
+                sP[(RA * ty + a) * (FA_BC + 4) + 4 * tx + b] = p;
             }
 #pragma unroll
             for (int off = 1; off < 16; off <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
@@ -260,25 +277,25 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
         }
         __syncthreads();
 #pragma unroll
-        for (int a = 0; a < 4; ++a)
+        for (int a = 0; a < RA; ++a)
 #pragma unroll
             for (int c = 0; c < DT; ++c) o[a][c] *= alpha[a];
 #pragma unroll 4
         for (int j = 0; j < FA_BC; ++j) {
-            float pv[4];
+            float pv[RA];
 #pragma unroll
-            for (int a = 0; a < 4; ++a) pv[a] = sP[(4 * ty + a) * (FA_BC + 4) + j];
+            for (int a = 0; a < RA; ++a) pv[a] = sP[(RA * ty + a) * (FA_BC + 4) + j];
 #pragma unroll
             for (int c = 0; c < DT; ++c) {
                 const float vv = sV[j * (DP + 4) + tx + 16 * c];
 #pragma unroll
-                for (int a = 0; a < 4; ++a) o[a][c] = fmaf(pv[a], vv, o[a][c]);
+                for (int a = 0; a < RA; ++a) o[a][c] = fmaf(pv[a], vv, o[a][c]);
             }
         }
     }
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
-        const int row = m0 + 4 * ty + a;
+    for (int a = 0; a < RA; ++a) {
+        const int row = m0 + RA * ty + a;
         if (row >= S) continue;
         const float inv = 1.0f / l_run[a];
 #pragma unroll
@@ -325,17 +342,37 @@ template cudaError_t conv2d_simt_launch<float>(float*, const float*, const float
 template cudaError_t conv2d_simt_launch<__nv_bfloat16>(float*, const __nv_bfloat16*, const __nv_bfloat16*, const float*,
                                                        const Conv2dShape&, cudaStream_t);
 
+template <typename T, int DT, int RA>
+static cudaError_t flash_attn_simt_launch_ra(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
+                                             cudaStream_t stream) {
+    constexpr int DP = 16 * DT, BR = 16 * RA;
+    const size_t smem = sizeof(float) * ((size_t)DP * (BR + 4) + (size_t)DP * (FA_BC + 4) + (size_t)FA_BC * (DP + 4) + (size_t)BR * (FA_BC + 4));
+    cudaError_t e = cudaFuncSetAttribute(flash_attn_simt_kernel<T, DT, RA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((S + BR - 1) / BR, B * H);
+    const float scale_log2 = scale * 1.4426950408889634f;  // scores in the exp2 domain
+    flash_attn_simt_kernel<T, DT, RA><<<grid, 256, smem, stream>>>(out, q, k, v, H, S, D, scale_log2, causal);
+    return cudaGetLastError();
+}
+
+// Rows per thread: 4 (64-row query tiles) when that gives at least one CTA per SM; else 2 when
+// 32-row tiles fill half the SMs; else 1. C3 (1 x 8 x 512 x 64): 64, 128 or 256 CTAs took 75.8,
+// 57.3 and 65.6 us; 1 x 4 x 300 x 40: 43.0, 30.7 and 29.7 us.
+static int flash_attn_simt_rows_per_thread(int B, int H, int S) {
+    const long long bh = static_cast<long long>(B) * H;
+    if ((S + 63) / 64 * bh >= 148) return 4;
+    if ((S + 31) / 32 * bh >= 74) return 2;
+    return 1;
+}
+
 template <typename T, int DT>
 static cudaError_t flash_attn_simt_launch_dt(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
                                              cudaStream_t stream) {
-    constexpr int DP = 16 * DT;
-    const size_t smem = sizeof(float) * ((size_t)2 * DP * (FA_BR + 4) + (size_t)FA_BC * (DP + 4) + (size_t)FA_BR * (FA_BC + 4));
-    cudaError_t e = cudaFuncSetAttribute(flash_attn_simt_kernel<T, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    dim3 grid((S + FA_BR - 1) / FA_BR, B * H);
-    const float scale_log2 = scale * 1.4426950408889634f;  // scores in the exp2 domain
-    flash_attn_simt_kernel<T, DT><<<grid, 256, smem, stream>>>(out, q, k, v, H, S, D, scale_log2, causal);
-    return cudaGetLastError();
+    switch (flash_attn_simt_rows_per_thread(B, H, S)) {
+        case 4: return flash_attn_simt_launch_ra<T, DT, 4>(out, q, k, v, B, H, S, D, scale, causal, stream);
+        case 2: return flash_attn_simt_launch_ra<T, DT, 2>(out, q, k, v, B, H, S, D, scale, causal, stream);
+        default: return flash_attn_simt_launch_ra<T, DT, 1>(out, q, k, v, B, H, S, D, scale, causal, stream);
+    }
 }
 
 template <typename T>
