@@ -256,7 +256,7 @@ int conv2d_tc_run(float* out, const void* input, const void* weight, const float
                                      stream));
     const void* w_ftc = static_cast<const char*>(scratch) + kg::conv2d_tc_weight_offset(t);
     CUtensorMap tx, tw;
-    const cuuint64_t xd[2] = {(cuuint64_t)t.Cp, (cuuint64_t)kg::conv_tc_rows(t)};
+    const cuuint64_t xd[2] = {(cuuint64_t)t.Cp, (cuuint64_t)kg::conv_tc_scratch_rows(t)};
     const cuuint64_t xs[1] = {(cuuint64_t)t.Cp * 2};
     const cuuint32_t xb[2] = {64, 128};
     const cuuint64_t wd[3] = {(cuuint64_t)t.Cp, (cuuint64_t)(t.KH * t.KW), (cuuint64_t)t.F};
@@ -942,6 +942,7 @@ extern "C" int kg_sm100_conv2d_noalloc(float* out, const void* input, const void
     int rc = conv2d_shape(&s, B, C, XH, XW, F, KH, KW, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_bottom, pad_left,
                           pad_right);
     if (rc != KG_OK) return rc;
+    if (s.sh != 1 || s.sw != 1) return fail(KG_ERR_UNSUPPORTED, "conv2d_noalloc: stride 1 only (got %d x %d)", s.sh, s.sw);
     const kg::ConvTcShape t = conv_tc_shape(s);
     if (!kg::conv2d_tc_supported(t)) return fail(KG_ERR_UNSUPPORTED, "conv2d_noalloc: only the tensor-core path (stride 1)");
     const size_t need = kg::conv2d_tc_scratch_bytes(t);

@@ -2,16 +2,19 @@
 //
 // Computes the reference conv2d loop nest (kernel/conv2d/inputs_dynamic_tile_dynamic.py:142-205:
 // out[b,f,ho,wo] = sum_{c,kh,kw} weight[f,c,kh,kw] * input[b,c,ho*sh-pt+kh*dh, wo*sw-pl+kw*dw],
-// zero outside the input) for bf16 inputs with f32 accumulation and f32 NCHW output, stride 1.
+// zero outside the input) for bf16 inputs with f32 accumulation and f32 NCHW output.
 //
 //   1. Repack (scratch): input NCHW -> x_pad [B, XHp, XWp, Cp] with the padding written as zero
 //      rows/columns (XHp = XH+pt+pb, XWp = XW+pl+pr) and channels padded to a multiple of 8;
-//      weights OIHW -> [F, KH*KW, Cp].
-//   2. GEMM rows = padded pixels p = (b*XHp + ho)*XWp + wo, columns = filters, reduction =
-//      (tap, 64-channel block). Output pixel (b, ho, wo) reads x_pad[b, ho+kh*dh, wo+kw*dw], which is
-//      row p + kh*dh*XWp + kw*dw of x_pad viewed as a [B*XHp*XWp, Cp] matrix: every tap's A tile is
-//      one 2-D TMA box of 128 consecutive rows, shifted. Rows with wo >= WO or ho >= HO are
-//      computed and dropped (for 56x56 outputs with pad 1: 3136 of 3364 rows kept, 93 %).
+//      weights OIHW -> [F, KH*KW, Cp]. With stride (sh, sw) > 1, x_pad is stored as sh*sw phase
+//      planes [B, XHq, XWq, Cp], plane (ph, pw) holding padded pixels (h'*sh + ph, w'*sw + pw).
+//   2. GEMM rows = pixels p = (b*XHq + ho)*XWq + wo of one plane (the padded image when the
+//      stride is 1), columns = filters, reduction = (tap, 64-channel block). Output pixel
+//      (b, ho, wo) reads x_pad[b, ho*sh+kh*dh, wo*sw+kw*dw]: plane ((kh*dh) % sh, (kw*dw) % sw),
+//      row p + ((kh*dh) / sh)*XWq + (kw*dw) / sw of it, so every tap's A tile is one 2-D TMA box
+//      of 128 consecutive rows of the planes viewed as a [rows, Cp] matrix, shifted. Rows with
+//      wo >= WO or ho >= HO are computed and dropped (for 56x56 outputs with pad 1: 3136 of 3364
+//      rows kept, 93 %).
 //   3. Epilogue: TMEM lane = pixel, so each filter column is a coalesced run of output pixels.
 //
 // Kernel structure as the pair GEMM (kg_gemm_tc2.cu): a cluster of 2 CTAs owns a 256-pixel x PBN-filter
@@ -87,10 +90,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const bool leader = rank == 0;
     const int pair = blockIdx.x >> 1;
     const int num_pairs = gridDim.x >> 1;
-    const int xhp = s.XH + s.pt + s.pb;
-    const int xwp = s.XW + s.pl + s.pr;
-    const int img = xhp * xwp;
-    const int rows = s.B * img;  // conv2d_tc_supported keeps this and every shifted row below 2^31
+    const int xwq = conv_tc_xwq(s);
+    const int img = conv_tc_xhq(s) * xwq;
+    const int rows = s.B * img;  // one plane; conv2d_tc_supported keeps every shifted row below 2^31
     const int num_m = (rows + PBM - 1) / PBM;
     const int num_n = (s.F + PBN - 1) / PBN;
     const int num_tiles = num_m * num_n;
@@ -144,11 +146,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                 conv_tile_coords(tile, num_m, num_n, mb, nb);
                 const int row0 = mb * PBM + static_cast<int>(rank) * 128;
                 const int f0 = nb * PBN + static_cast<int>(rank) * Cfg::BNC;
+                // (tap, channel block) of k-step kidx, walked without divisions: the tap's row shift
+                // (plane offset included) is recomputed only when the tap changes.
+                int cb = 0, kh = 0, kw = 0, shift = 0;
                 for (int kidx = 0; kidx < num_k; ++kidx) {
-                    const int tap = kidx / c_blocks;
-                    const int cb = kidx - tap * c_blocks;
-                    const int kh = tap / s.KW, kw = tap - kh * s.KW;
-                    const int shift = kh * s.dh * xwp + kw * s.dw;
+                    if (kidx > 0 && ++cb == c_blocks) {
+                        cb = 0;
+                        if (++kw == s.KW) {
+                            kw = 0;
+                            ++kh;
+                        }
+                        const int dy = kh * s.dh, dx = kw * s.dw;
+                        shift = ((dy % s.sh) * s.sw + dx % s.sw) * rows + (dy / s.sh) * xwq + dx / s.sw;
+                    }
+                    const int tap = kh * s.KW + kw;
                     if (!mbar_wait_cluster(&bars->empty[stage], phase ^ 1u, abort, status, kDevTimeoutProducer)) break;
                     if (leader) mbar_arrive_expect_tx(&bars->full[stage], 2 * (A_STAGE_BYTES + Cfg::B_STAGE_BYTES));
                     const uint32_t leader_full = mapa_shared(smem_u32(&bars->full[stage]), 0);
@@ -243,8 +254,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                 const int p = pg + i;
                 const int b = p / img;
                 const int rem = p - b * img;
-                const int ho = rem / xwp;
-                const int wo = rem - ho * xwp;
+                const int ho = rem / xwq;
+                const int wo = rem - ho * xwq;
                 off[i] = static_cast<size_t>(b) * s.F * plane + static_cast<size_t>(ho) * s.WO + wo;
                 if (p < rows && ho < s.HO && wo < s.WO) valid |= 1u << i;
             }
@@ -327,6 +338,7 @@ constexpr int RP_PIX = 64, RP_CH = 64, RP_ROWS = 2;
 constexpr int RP_TASKS = RP_ROWS * RP_CH * (RP_PIX / 8) / 256;  // 8-pixel loads per thread per chunk
 __device__ __forceinline__ int rp_col(int px, int c) { return c ^ (((px >> 3) & 7) << 3); }
 
+template <bool PHASED>
 __global__ void __launch_bounds__(256, 6) conv_repack_kernel(__nv_bfloat16* __restrict__ x_pad, const __nv_bfloat16* __restrict__ src,
                                                           __nv_bfloat16* __restrict__ w_ftc, const __nv_bfloat16* __restrict__ weight,
                                                           ConvTcShape s, int vec_ok, int x_blocks) {
@@ -356,24 +368,33 @@ __global__ void __launch_bounds__(256, 6) conv_repack_kernel(__nv_bfloat16* __re
     const int c0 = static_cast<int>(blockIdx.y) * RP_CH;
     const int nvec = min(RP_CH, s.Cp - c0) / 8;  // 16-byte channel groups this block writes
     const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
-    auto row_ptr = [&](int hp) { return x_pad + (static_cast<size_t>(b) * xhp + hp) * xwp * s.Cp + c0; };
+    // Scratch address of padded pixel (hp, wp) of image b, channel c0: one padded image, or (PHASED)
+    // position (hp / sh, wp / sw) of phase plane (hp % sh, wp % sw).
+    auto px_ptr = [&](int hp, int wp) {
+        if constexpr (PHASED) {
+            const int plane = (hp % s.sh) * s.sw + wp % s.sw;
+            const int xhq = conv_tc_xhq(s), xwq = conv_tc_xwq(s);
+            return x_pad + ((static_cast<size_t>(plane) * s.B + b) * xhq + hp / s.sh) * xwq * s.Cp + static_cast<size_t>(wp / s.sw) * s.Cp + c0;
+        } else {
+            return x_pad + ((static_cast<size_t>(b) * xhp + hp) * xwp + wp) * s.Cp + c0;
+        }
+    };
     auto data_row = [&](int hp) { return hp < xhp && hp - s.pt >= 0 && hp - s.pt < s.XH; };
     // border rows (all columns) and border columns of data rows
 #pragma unroll
     for (int r = 0; r < RP_ROWS; ++r) {
         const int hp = hp0 + r;
         if (hp >= xhp) break;
-        __nv_bfloat16* row = row_ptr(hp);
         if (!data_row(hp)) {
             for (int i = threadIdx.x; i < xwp * nvec; i += 256) {
                 const int px = i / nvec, v = i - px * nvec;
-                *reinterpret_cast<uint4*>(row + static_cast<size_t>(px) * s.Cp + 8 * v) = zero4;
+                *reinterpret_cast<uint4*>(px_ptr(hp, px) + 8 * v) = zero4;
             }
         } else {
             for (int i = threadIdx.x; i < (s.pl + s.pr) * nvec; i += 256) {
                 const int k = i / nvec, v = i - k * nvec;
                 const int px = k < s.pl ? k : s.XW + k;  // left border columns, then right ones
-                *reinterpret_cast<uint4*>(row + static_cast<size_t>(px) * s.Cp + 8 * v) = zero4;
+                *reinterpret_cast<uint4*>(px_ptr(hp, px) + 8 * v) = zero4;
             }
         }
     }
@@ -417,8 +438,7 @@ __global__ void __launch_bounds__(256, 6) conv_repack_kernel(__nv_bfloat16* __re
             const int px = rem / nvec, v = rem - px * nvec;
             const int hp = hp0 + r;
             if (!data_row(hp)) continue;
-            *reinterpret_cast<uint4*>(row_ptr(hp) + static_cast<size_t>(s.pl + w0 + px) * s.Cp + 8 * v) =
-                *reinterpret_cast<const uint4*>(&tile[r][px][rp_col(px, 8 * v)]);
+            *reinterpret_cast<uint4*>(px_ptr(hp, s.pl + w0 + px) + 8 * v) = *reinterpret_cast<const uint4*>(&tile[r][px][rp_col(px, 8 * v)]);
         }
         __syncthreads();
     }
@@ -441,9 +461,9 @@ cudaError_t launch_pbn(const CUtensorMap& tm_x, const CUtensorMap& tm_w, float* 
     const long long num_tiles = ((conv_tc_rows(s) + PBM - 1) / PBM) * ((s.F + PBN - 1) / PBN);
     const long long max_pairs = num_sms / 2 > 0 ? num_sms / 2 : 1;
     const int pairs = static_cast<int>(num_tiles < max_pairs ? num_tiles : max_pairs);
-    // float4 stores need 16-byte aligned output rows and 4-pixel groups that never straddle a padded row
-    const int xwp = conv_tc_xwp(s);
-    const int vec_ok = (s.WO % 4) == 0 && (xwp % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
+    // float4 stores need 16-byte aligned output rows and 4-pixel groups that never straddle a plane row
+    const int xwq = conv_tc_xwq(s);
+    const int vec_ok = (s.WO % 4) == 0 && (xwq % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0;
     // Programmatic dependent launch: the CTAs' setup (barriers, TMEM, descriptor prefetch) overlaps
     // the tail of the repack before it on the stream.
     cudaLaunchConfig_t cfg = {};
@@ -462,18 +482,20 @@ cudaError_t launch_pbn(const CUtensorMap& tm_x, const CUtensorMap& tm_w, float* 
 }  // namespace
 
 bool conv2d_tc_supported(const ConvTcShape& s) {
+    if (s.sh < 1 || s.sw < 1 || s.sh > 8 || s.sw > 8) return false;
     const long long xhp = conv_tc_xhp(s), xwp = conv_tc_xwp(s);
-    const long long max_shift = static_cast<long long>(s.KH - 1) * s.dh * xwp + static_cast<long long>(s.KW - 1) * s.dw;
+    const long long max_shift = (conv_tc_planes(s) - 1) * conv_tc_rows(s) + static_cast<long long>(s.KH - 1) * s.dh / s.sh * conv_tc_xwq(s) +
+                                static_cast<long long>(s.KW - 1) * s.dw / s.sw;
     const long long rows = conv_tc_rows(s);
     const long long tiles = (rows + PBM - 1) / PBM * ((s.F + 63) / 64);
-    return s.sh == 1 && s.sw == 1 && s.B > 0 && s.F > 0 && s.Cp > 0 && s.Cp % 8 == 0 && xhp > 0 && xwp > 0 &&
-           rows + PBM + max_shift < (1LL << 31) && tiles < (1LL << 31) && (s.Cp + 63) / 64 <= 65535;
+    return s.B > 0 && s.F > 0 && s.Cp > 0 && s.Cp % 8 == 0 && xhp > 0 && xwp > 0 && rows + PBM + max_shift < (1LL << 31) &&
+           conv_tc_scratch_rows(s) < (1LL << 31) && tiles < (1LL << 31) && (s.Cp + 63) / 64 <= 65535;
 }
 
 int conv2d_tc_block_n(int F) { return F <= 64 ? 64 : (F <= 128 ? 128 : 256); }
 
 size_t conv2d_tc_weight_offset(const ConvTcShape& s) {
-    return (static_cast<size_t>(conv_tc_rows(s)) * s.Cp * 2 + 255) & ~size_t(255);
+    return (static_cast<size_t>(conv_tc_scratch_rows(s)) * s.Cp * 2 + 255) & ~size_t(255);
 }
 
 size_t conv2d_tc_scratch_bytes(const ConvTcShape& s) {
@@ -490,7 +512,10 @@ cudaError_t conv2d_tc_repack(void* scratch, const __nv_bfloat16* input, const __
     if (x_blocks + w_blocks >= (1LL << 31)) return cudaErrorInvalidValue;
     const int vec_ok = (s.XW % 8) == 0 && (reinterpret_cast<uintptr_t>(input) & 15u) == 0;
     dim3 grid(static_cast<unsigned>(x_blocks + w_blocks), (s.Cp + RP_CH - 1) / RP_CH);
-    conv_repack_kernel<<<grid, 256, 0, stream>>>(x_pad, input, w_ftc, weight, s, vec_ok, static_cast<int>(x_blocks));
+    if (s.sh == 1 && s.sw == 1)
+        conv_repack_kernel<false><<<grid, 256, 0, stream>>>(x_pad, input, w_ftc, weight, s, vec_ok, static_cast<int>(x_blocks));
+    else
+        conv_repack_kernel<true><<<grid, 256, 0, stream>>>(x_pad, input, w_ftc, weight, s, vec_ok, static_cast<int>(x_blocks));
     return cudaGetLastError();
 }
 

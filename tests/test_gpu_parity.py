@@ -497,17 +497,36 @@ def test_bf16_conv2d_tensor_cores_vs_oracle(cuda_device, x_shape, f, k, stride, 
     np.testing.assert_allclose(out.cpu().numpy(), expect, **BF16_TOL)
 
 
-def test_bf16_conv2d_strided_uses_cuda_cores(cuda_device):
+@pytest.mark.parametrize("x_shape,f,k,stride,dilation,pads,with_bias", [
+    ((1, 8, 17, 19), 12, (3, 3), (2, 2), (1, 1), (1, 1, 1, 1), False),       # odd padded extents: partial last plane rows
+    ((2, 64, 56, 56), 128, (3, 3), (2, 2), (1, 1), (1, 1, 1, 1), True),      # downsampling 3x3, WO % 4 == 0 (float4 path)
+    ((1, 32, 30, 30), 64, (1, 1), (2, 2), (1, 1), (0, 0, 0, 0), False),      # 1x1 projection, WO = 15
+    ((1, 16, 23, 41), 40, (5, 5), (3, 3), (1, 1), (2, 2, 2, 2), True),       # stride 3: nine planes
+    ((2, 24, 20, 33), 72, (3, 3), (2, 1), (2, 1), (1, 2, 0, 1), True),       # mixed stride, dilation, asymmetric pads
+    ((1, 3, 64, 64), 32, (7, 7), (2, 2), (1, 1), (3, 3, 3, 3), False),       # stem: C = 3, 7x7
+    ((1, 40, 12, 300), 264, (3, 3), (1, 2), (1, 1), (1, 1, 1, 1), True),     # stride only along W, F > 256, several row tiles
+])
+def test_bf16_conv2d_strided_tensor_cores_vs_oracle(cuda_device, x_shape, f, k, stride, dilation, pads, with_bias):
+    """Strides > 1 on tensor cores through phase planes of the padded input; whole result vs the
+    oracle, and the same result from a second call (the planes' unwritten positions do not leak)."""
     torch = _torch()
-    rng = np.random.default_rng(5)
-    x = workloads.bf16_bits(rng.uniform(-1, 1, (1, 8, 17, 19)).astype(np.float32))
-    w = workloads.bf16_bits(rng.standard_normal((12, 8, 3, 3), dtype=np.float32) / np.float32(8.0))
-    expect = oracle.conv2d(x, w, None, stride=(2, 2), dilation=(1, 1), pads=(1, 1, 1, 1), tiles=(8, 16, 4, 8, 9))
-    out = torch.empty(expect.shape, device=cuda_device)
-    kernels.conv2d(out, _to_torch(x, cuda_device), _to_torch(w, cuda_device), None, (2, 2), (1, 1), (1, 1, 1, 1))
+    rng = np.random.default_rng(sum(x_shape) + f + 7 * stride[0] + stride[1])
+    x = workloads.bf16_bits(rng.uniform(-1, 1, x_shape).astype(np.float32))
+    w = workloads.bf16_bits((rng.standard_normal((f, x_shape[1], *k), dtype=np.float32) / np.float32(np.sqrt(x_shape[1] * k[0] * k[1]))))
+    bias = rng.standard_normal(f, dtype=np.float32) if with_bias else None
+    expect = oracle.conv2d(x, w, bias, stride=stride, dilation=dilation, pads=pads, tiles=(8, 16, 4, 8, 9))
+    args = (_to_torch(x, cuda_device), _to_torch(w, cuda_device), None if bias is None else _to_torch(bias, cuda_device), stride,
+            dilation, pads)
+    out = torch.full(expect.shape, float("nan"), device=cuda_device)
+    kernels.conv2d(out, *args)
     torch.cuda.synchronize()
-    assert runtime.last_kernel() == "conv2d_simt_kernel<bf16>"
+    assert runtime.last_kernel() == "conv2d_tc_kernel"
+    assert runtime.device_status() == 0
     np.testing.assert_allclose(out.cpu().numpy(), expect, **BF16_TOL)
+    again = torch.full_like(out, float("nan"))
+    kernels.conv2d(again, *args)
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)
 
 
 def test_engine_execute_on_a_stream_matches_the_synchronous_entry(cuda_device):

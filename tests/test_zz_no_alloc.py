@@ -83,3 +83,9 @@ def test_noalloc_conv2d_refuses_shapes_beyond_its_array(cuda_device):
     rc = noalloc(f32.data_ptr(), f32.data_ptr(), f32.data_ptr(), runtime.KG_DTYPE_F32, None, 1, 8, 8, 8, 8, 1, 1, 1, 1, 1, 1, 0, 0, 0, 0,
                  None)
     assert rc == runtime.KG_ERR_UNSUPPORTED
+    # strides other than 1 stay refused here (the allocating entry runs them on tensor cores)
+    small = torch.zeros((1, 8, 16, 16), dtype=torch.bfloat16, device=cuda_device)
+    w3 = torch.zeros((8, 8, 3, 3), dtype=torch.bfloat16, device=cuda_device)
+    out2 = torch.zeros((1, 8, 8, 8), device=cuda_device)
+    rc = noalloc(*_conv_args(out2, small, w3, None, (2, 2), (1, 1), (1, 1, 1, 1)))
+    assert rc == runtime.KG_ERR_UNSUPPORTED and "stride" in runtime.last_error()
