@@ -409,7 +409,8 @@ unsigned long long launches_of(const char* kernel) { return std::strcmp(kernel, 
 
 // Runs one *_impl call (its kernels back to back on `s`), timed with an event pair when a cost
 // capture is active.
-int cost_timed(cudaStream_t s, const std::function<int()>& launch) {
+template <class Launch>
+int cost_timed(cudaStream_t s, Launch&& launch) {
     if (t_cost == nullptr) return launch();
     cudaEvent_t a = cost_event(), b = cost_event();
     if (a != nullptr && cudaEventRecord(a, s) != cudaSuccess) t_cost->event_failed = true;
