@@ -131,7 +131,9 @@ KG_API int kg_sm100_flash_attention_capture(const KgArgSlot* ordered_args, unsig
 KG_API int kg_sm100_matmul(float* out, const void* lhs, const void* rhs, int in_dtype, const float* bias,
                     long long M, long long K, long long N, void* stream);
 
-/* NCHW conv2d: out[B,F,HO,WO] (f32) with HO = (XH+pt+pb-dh*(KH-1)-1)/sh+1, WO likewise. */
+/* NCHW conv2d: out[B,F,HO,WO] (f32) with HO = (XH+pt+pb-dh*(KH-1)-1)/sh+1, WO likewise. bf16 runs
+ * on tcgen05 tensor cores for any stride and dilation (a repack into device scratch first), f32 on
+ * exact FFMA. */
 KG_API int kg_sm100_conv2d(float* out, const void* input, const void* weight, int in_dtype, const float* bias,
                     long long B, long long C, long long XH, long long XW, long long F, long long KH, long long KW,
                     long long stride_h, long long stride_w, long long dilation_h, long long dilation_w,
