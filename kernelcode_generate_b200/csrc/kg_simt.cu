@@ -93,6 +93,48 @@ __global__ void __launch_bounds__(256) matmul_simt_kernel(float* __restrict__ ou
     }
 }
 
+// Small problems (fewer 32x32 tiles than SMs, K <= PANEL_KMAX): 16 x 16 output tile per CTA, one
+// output per thread, and the CTA's whole A and B panels (16 x K and K x 16) staged in shared
+// memory after ONE round of global loads: every thread first loads all of its panel elements into
+// registers, then stores them, so the cold-cache latency is paid once instead of once per K step.
+// Each output accumulates k = 0..K-1 in order, as the tiled kernel above does.
+constexpr int PANEL_KMAX = 512;
+constexpr int PANEL_LDA = 17;  // transposed A panel pitch: the stores of consecutive k hit distinct banks
+
+template <typename T>
+__global__ void __launch_bounds__(256) matmul_simt_panel_kernel(float* __restrict__ out, const T* __restrict__ lhs, const T* __restrict__ rhs,
+                                                                const float* __restrict__ bias, int M, int N, int K) {
+    extern __shared__ float panel_smem[];
+    float* sa = panel_smem;              // [K][PANEL_LDA]: sa[k * PANEL_LDA + r] = lhs[m0 + r, k]
+    float* sb = sa + K * PANEL_LDA;      // [K][16]:        sb[k * 16 + c] = rhs[k, n0 + c]
+    constexpr int PER = PANEL_KMAX * 16 / 256;
+    const int m0 = blockIdx.y * 16, n0 = blockIdx.x * 16;
+    float va[PER], vb[PER];
+    // Element j of this thread: A row r = t / 16, column c = t % 16 + 16 j (16 threads read 16
+    // consecutive k of a row); B row k = t / 16 + 16 j, column t % 16 (16 consecutive columns).
+    const int r = threadIdx.x >> 4, c0 = threadIdx.x & 15;
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int kk = c0 + 16 * j, kb = r + 16 * j;
+        va[j] = vb[j] = 0.0f;
+        if (kk < K && m0 + r < M) va[j] = to_f32(lhs[(size_t)(m0 + r) * K + kk]);
+        if (kb < K && n0 + c0 < N) vb[j] = to_f32(rhs[(size_t)kb * N + n0 + c0]);
+    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+        const int kk = c0 + 16 * j, kb = r + 16 * j;
+        if (kk < K) sa[kk * PANEL_LDA + r] = va[j];
+        if (kb < K) sb[kb * 16 + c0] = vb[j];
+    }
+    __syncthreads();
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int k = 0; k < K; ++k) acc = fmaf(sa[k * PANEL_LDA + ty], sb[k * 16 + tx], acc);
+    const int gm = m0 + ty, gn = n0 + tx;
+    if (gm < M && gn < N) out[(size_t)gm * N + gn] = acc + (bias ? bias[gn] : 0.0f);
+}
+
 // ------------------------------------------------------------------ conv2d implicit GEMM
 // GEMM rows = output channels f, columns = (b, ho, wo), reduction = (c, kh, kw) in the
 // reference's weight2 / col2 order (OIHW flattening).
@@ -311,7 +353,16 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
 template <typename T>
 cudaError_t matmul_simt_launch(float* out, const T* lhs, const T* rhs, const float* bias, int M, int N, int K, cudaStream_t stream) {
     const long long big_tiles = (long long)((N + 63) / 64) * ((M + 63) / 64);
-    if (big_tiles >= 148) {
+    const long long small_tiles = (long long)((N + 31) / 32) * ((M + 31) / 32);
+    if (small_tiles < 148 && K <= PANEL_KMAX) {
+        const size_t smem = sizeof(float) * (size_t)K * (PANEL_LDA + 16);
+        if (smem > 48 * 1024) {
+            cudaError_t e = cudaFuncSetAttribute(matmul_simt_panel_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+        }
+        dim3 grid((N + 15) / 16, (M + 15) / 16);
+        matmul_simt_panel_kernel<T><<<grid, 256, smem, stream>>>(out, lhs, rhs, bias, M, N, K);
+    } else if (big_tiles >= 148) {
         dim3 grid((N + 63) / 64, (M + 63) / 64);
         matmul_simt_kernel<T, 64, 64, 16><<<grid, 256, 0, stream>>>(out, lhs, rhs, bias, M, N, K);
     } else {
