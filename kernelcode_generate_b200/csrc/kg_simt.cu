@@ -139,11 +139,14 @@ __global__ void __launch_bounds__(256) matmul_simt_panel_kernel(float* __restric
 // GEMM rows = output channels f, columns = (b, ho, wo), reduction = (c, kh, kw) in the
 // reference's weight2 / col2 order (OIHW flattening).
 // CV_BM output channels x CV_BN output pixels per CTA; 256 threads as 8 (channels) x 32 (pixels),
-// each (CV_BM/8) x (CV_BN/32) outputs. Small problems use 16 x 32 tiles with K steps of 48.
+// each (CV_BM/8) x (CV_BN/32) outputs. Small problems use 16 x 32 tiles with K steps of 48, or
+// of 144 when the reduction is deeper than 48.
 template <typename T, int CV_BM, int CV_BN, int CV_BK>
 __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ out, const T* __restrict__ input, const T* __restrict__ weight,
                                                           const float* __restrict__ bias, Conv2dShape s) {
     constexpr int TM = CV_BM / 8, TN = CV_BN / 32;
+    constexpr int W_PER = CV_BM * CV_BK / 256, X_PER = CV_BK * CV_BN / 256;  // elements per thread and K step
+    static_assert(W_PER * 256 == CV_BM * CV_BK && X_PER * 256 == CV_BK * CV_BN, "whole elements per thread");
     __shared__ float sw[CV_BK][CV_BM + 1];
     __shared__ float sx[CV_BK][CV_BN + 4];
     const int Kred = s.C * s.KH * s.KW;
@@ -154,12 +157,18 @@ __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ ou
     const int ty = threadIdx.x >> 5;  // rows ty + 8 i
     float acc[TM][TN] = {};
     for (int k0 = 0; k0 < Kred; k0 += CV_BK) {
-        for (int i = threadIdx.x; i < CV_BM * CV_BK; i += 256) {
+        // All of this step's loads are issued before any store, so their latencies overlap.
+        float wv[W_PER], xv[X_PER];
+#pragma unroll
+        for (int e = 0; e < W_PER; ++e) {
+            const int i = threadIdx.x + 256 * e;
             const int r = i / CV_BK, c = i % CV_BK;
             const int f = f0 + r, kk = k0 + c;
-            sw[c][r] = (f < s.F && kk < Kred) ? to_f32(weight[(size_t)f * Kred + kk]) : 0.0f;
+            wv[e] = (f < s.F && kk < Kred) ? to_f32(weight[(size_t)f * Kred + kk]) : 0.0f;
         }
-        for (int i = threadIdx.x; i < CV_BK * CV_BN; i += 256) {
+#pragma unroll
+        for (int e = 0; e < X_PER; ++e) {
+            const int i = threadIdx.x + 256 * e;
             const int r = i / CV_BN, c = i % CV_BN;
             const int kk = k0 + r;
             const long long col = n0 + c;
@@ -179,7 +188,17 @@ __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ ou
                     v = to_f32(input[(((size_t)b * s.C + ci) * s.XH + h) * s.XW + w]);
                 }
             }
-            sx[r][c] = v;
+            xv[e] = v;
+        }
+#pragma unroll
+        for (int e = 0; e < W_PER; ++e) {
+            const int i = threadIdx.x + 256 * e;
+            sw[i % CV_BK][i / CV_BK] = wv[e];
+        }
+#pragma unroll
+        for (int e = 0; e < X_PER; ++e) {
+            const int i = threadIdx.x + 256 * e;
+            sx[i / CV_BN][i % CV_BN] = xv[e];
         }
         __syncthreads();
 #pragma unroll
@@ -383,9 +402,12 @@ cudaError_t conv2d_simt_launch(float* out, const T* input, const T* weight, cons
     if (big_tiles >= 148) {
         dim3 grid((unsigned)((ncols + 63) / 64), (s.F + 31) / 32);
         conv2d_simt_kernel<T, 32, 64, 16><<<grid, 256, 0, stream>>>(out, input, weight, bias, s);
-    } else {
+    } else if (static_cast<long long>(s.C) * s.KH * s.KW <= 48) {
         dim3 grid((unsigned)((ncols + 31) / 32), (s.F + 15) / 16);
         conv2d_simt_kernel<T, 16, 32, 48><<<grid, 256, 0, stream>>>(out, input, weight, bias, s);
+    } else {  // small grid, deeper reduction: K steps of 144 (one step for 16 channels x 3 x 3)
+        dim3 grid((unsigned)((ncols + 31) / 32), (s.F + 15) / 16);
+        conv2d_simt_kernel<T, 16, 32, 144><<<grid, 256, 0, stream>>>(out, input, weight, bias, s);
     }
     return cudaGetLastError();
 }
