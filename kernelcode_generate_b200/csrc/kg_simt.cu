@@ -287,11 +287,29 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
     const int n_end = causal ? min(S, m0 + BR) : S;
     for (int n0 = 0; n0 < n_end; n0 += FA_BC) {
         __syncthreads();
-        for (int i = threadIdx.x; i < FA_BC * DP; i += 256) {
-            const int j = i / DP, d = i - j * DP;
-            const bool ok = n0 + j < S && d < D;
-            sKt[d * LDK + j] = ok ? to_f32(k[base + (size_t)(n0 + j) * D + d]) : 0.0f;
-            sV[j * (DP + 4) + d] = ok ? to_f32(v[base + (size_t)(n0 + j) * D + d]) : 0.0f;
+        // K and V tile: KV_PER elements of each per thread, loaded in chunks whose loads are all
+        // issued before their shared-memory stores, so their latencies overlap.
+        constexpr int KV_PER = FA_BC * DP / 256;
+        constexpr int KV_CH = KV_PER <= 16 ? KV_PER : KV_PER / 2;  // KV_PER = 4 * DT <= 32
+        static_assert(KV_PER % KV_CH == 0, "whole chunks");
+#pragma unroll
+        for (int e0 = 0; e0 < KV_PER; e0 += KV_CH) {
+            float kv[KV_CH], vv[KV_CH];
+#pragma unroll
+            for (int e = 0; e < KV_CH; ++e) {
+                const int i = threadIdx.x + 256 * (e0 + e);
+                const int j = i / DP, d = i - j * DP;
+                const bool ok = n0 + j < S && d < D;
+                kv[e] = ok ? to_f32(k[base + (size_t)(n0 + j) * D + d]) : 0.0f;
+                vv[e] = ok ? to_f32(v[base + (size_t)(n0 + j) * D + d]) : 0.0f;
+            }
+#pragma unroll
+            for (int e = 0; e < KV_CH; ++e) {
+                const int i = threadIdx.x + 256 * (e0 + e);
+                const int j = i / DP, d = i - j * DP;
+                sKt[d * LDK + j] = kv[e];
+                sV[j * (DP + 4) + d] = vv[e];
+            }
         }
         __syncthreads();
         float sc[RA][4] = {};
