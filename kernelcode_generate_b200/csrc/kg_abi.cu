@@ -246,6 +246,17 @@ kg::ConvTcShape conv_tc_shape(const kg::Conv2dShape& s) {
     // pixel reads) so the padded row pitch is one too: the epilogue then stores 4-pixel float4 groups.
     const int xwp = s.XW + s.pl + s.pr;
     if (s.WO % 4 == 0) t.pr += (4 - xwp % 4) % 4;
+    // Few channels (a network's first layer): when the KW horizontal taps of all channels fit one
+    // 64-deep k-block, the repack folds them into the channel dimension, so each kernel row is one
+    // k-block instead of KW mostly-empty ones.
+    if (t.KW > 1 && t.Cp * t.KW <= 64) {
+        t.fold_kw = t.KW;
+        t.fold_cpc = t.Cp;
+        t.fold_dw = t.dw;
+        t.Cp = t.Cp * t.KW;
+        t.KW = 1;
+        t.dw = 1;
+    }
     return t;
 }
 

@@ -444,6 +444,55 @@ __global__ void __launch_bounds__(256, 6) conv_repack_kernel(__nv_bfloat16* __re
     }
 }
 
+// Repack with the horizontal taps folded into channels (ConvTcShape::fold_kw > 1): one thread per
+// (padded pixel, 8-channel group) of the scratch, gathering its 8 channels of one tap from the
+// NCHW input (zero in the padding and past the input), then one thread per (filter, channel) of
+// the [F, KH, Cp] weights. Used for few input channels, where the input is small.
+template <bool PHASED>
+__global__ void __launch_bounds__(256) conv_repack_fold_kernel(__nv_bfloat16* __restrict__ x_pad, const __nv_bfloat16* __restrict__ src,
+                                                               __nv_bfloat16* __restrict__ w_ftc, const __nv_bfloat16* __restrict__ weight,
+                                                               ConvTcShape s, long long x_items) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int groups = s.Cp / 8;
+    if (i < x_items) {
+        const int xhp = conv_tc_xhp(s), xwp = conv_tc_xwp(s);
+        const int g = static_cast<int>(i % groups);
+        long long px = i / groups;
+        const int wp = static_cast<int>(px % xwp);
+        px /= xwp;
+        const int hp = static_cast<int>(px % xhp);
+        const int b = static_cast<int>(px / xhp);
+        const int kw = 8 * g / s.fold_cpc, c0 = 8 * g - kw * s.fold_cpc;
+        const int h = hp - s.pt, w = wp + kw * s.fold_dw - s.pl;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&v);
+        if (kw < s.fold_kw && h >= 0 && h < s.XH && w >= 0 && w < s.XW) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (c0 + j < s.C) e[j] = src[((static_cast<size_t>(b) * s.C + c0 + j) * s.XH + h) * s.XW + w];
+        }
+        size_t pix;
+        if constexpr (PHASED) {
+            const int plane = (hp % s.sh) * s.sw + wp % s.sw;
+            pix = ((static_cast<size_t>(plane) * s.B + b) * conv_tc_xhq(s) + hp / s.sh) * conv_tc_xwq(s) + wp / s.sw;
+        } else {
+            pix = (static_cast<size_t>(b) * xhp + hp) * xwp + wp;
+        }
+        *reinterpret_cast<uint4*>(x_pad + pix * s.Cp + 8 * g) = v;
+        return;
+    }
+    const long long j = i - x_items;
+    if (j >= static_cast<long long>(s.F) * s.Cp) return;
+    const int f = static_cast<int>(j / s.Cp), cc = static_cast<int>(j % s.Cp);
+    const int kw = cc / s.fold_cpc, c = cc - kw * s.fold_cpc;
+    for (int kh = 0; kh < s.KH; ++kh) {
+        const bool ok = kw < s.fold_kw && c < s.C;
+        w_ftc[(static_cast<size_t>(f) * s.KH + kh) * s.Cp + cc] =
+            ok ? weight[((static_cast<size_t>(f) * s.C + c) * s.KH + kh) * s.fold_kw + kw] : __float2bfloat16(0.0f);
+    }
+}
+
 template <int PBN>
 cudaError_t launch_pbn(const CUtensorMap& tm_x, const CUtensorMap& tm_w, float* out, const float* bias, const ConvTcShape& s, int num_sms,
                        int* status, cudaStream_t stream) {
@@ -506,6 +555,17 @@ cudaError_t conv2d_tc_repack(void* scratch, const __nv_bfloat16* input, const __
                              cudaStream_t stream) {
     __nv_bfloat16* x_pad = static_cast<__nv_bfloat16*>(scratch);
     __nv_bfloat16* w_ftc = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(scratch) + conv2d_tc_weight_offset(s));
+    if (s.fold_kw > 1) {
+        const long long x_items = static_cast<long long>(s.B) * conv_tc_xhp(s) * conv_tc_xwp(s) * (s.Cp / 8);
+        const long long items = x_items + static_cast<long long>(s.F) * s.Cp;
+        if ((items + 255) / 256 >= (1LL << 31)) return cudaErrorInvalidValue;
+        const unsigned blocks = static_cast<unsigned>((items + 255) / 256);
+        if (s.sh == 1 && s.sw == 1)
+            conv_repack_fold_kernel<false><<<blocks, 256, 0, stream>>>(x_pad, input, w_ftc, weight, s, x_items);
+        else
+            conv_repack_fold_kernel<true><<<blocks, 256, 0, stream>>>(x_pad, input, w_ftc, weight, s, x_items);
+        return cudaGetLastError();
+    }
     const long long x_blocks = static_cast<long long>(s.B) * ((conv_tc_xhp(s) + RP_ROWS - 1) / RP_ROWS);
     const long long wtotal = static_cast<long long>(s.F) * s.Cp;
     const long long w_blocks = (wtotal + 255) / 256 < 1024 ? (wtotal + 255) / 256 : 1024;

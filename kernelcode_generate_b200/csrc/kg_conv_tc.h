@@ -12,6 +12,11 @@ struct ConvTcShape {
     int F, KH, KW, HO, WO;     // weight [F, C, KH, KW]; output [B, F, HO, WO]
     int sh, sw, dh, dw;        // stride, dilation
     int pt, pb, pl, pr;        // padding
+    // Horizontal taps folded into channels (few input channels): with fold_kw > 1 the scratch pixel
+    // (hp, wp) holds channel kw*fold_cpc + c = padded pixel (hp, wp + kw*fold_dw), input channel c,
+    // for kw < fold_kw, c < fold_cpc (C rounded up to 8); Cp = fold_kw * fold_cpc, and the kernel
+    // sees a KH x 1 convolution (KW = 1, dw = 1).
+    int fold_kw = 1, fold_cpc = 0, fold_dw = 1;
 };
 
 // Padded image extents (XHp, XWp) of the NHWC scratch.

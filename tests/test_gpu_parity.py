@@ -505,10 +505,13 @@ def test_bf16_conv2d_tensor_cores_vs_oracle(cuda_device, x_shape, f, k, stride, 
     ((2, 24, 20, 33), 72, (3, 3), (2, 1), (2, 1), (1, 2, 0, 1), True),       # mixed stride, dilation, asymmetric pads
     ((1, 3, 64, 64), 32, (7, 7), (2, 2), (1, 1), (3, 3, 3, 3), False),       # stem: C = 3, 7x7
     ((1, 40, 12, 300), 264, (3, 3), (1, 2), (1, 1), (1, 1, 1, 1), True),     # stride only along W, F > 256, several row tiles
+    ((1, 8, 15, 17), 24, (5, 3), (1, 2), (1, 2), (2, 2, 2, 2), True),        # taps folded into channels (8 x 3) with W stride and dilation
+    ((2, 3, 32, 32), 16, (3, 3), (1, 1), (1, 1), (1, 1, 1, 1), False),       # folded 3 x 3 stem, WO % 4 == 0 (float4 stores)
 ])
 def test_bf16_conv2d_strided_tensor_cores_vs_oracle(cuda_device, x_shape, f, k, stride, dilation, pads, with_bias):
-    """Strides > 1 on tensor cores through phase planes of the padded input; whole result vs the
-    oracle, and the same result from a second call (the planes' unwritten positions do not leak)."""
+    """Strides > 1 on tensor cores through phase planes of the padded input (and, for few
+    channels, with the horizontal taps folded into channels); whole result vs the oracle, and the
+    same result from a second call (the planes' unwritten positions do not leak)."""
     torch = _torch()
     rng = np.random.default_rng(sum(x_shape) + f + 7 * stride[0] + stride[1])
     x = workloads.bf16_bits(rng.uniform(-1, 1, x_shape).astype(np.float32))
