@@ -338,7 +338,9 @@ constexpr int RP_PIX = 64, RP_CH = 64, RP_ROWS = 2;
 constexpr int RP_TASKS = RP_ROWS * RP_CH * (RP_PIX / 8) / 256;  // 8-pixel loads per thread per chunk
 __device__ __forceinline__ int rp_col(int px, int c) { return c ^ (((px >> 3) & 7) << 3); }
 
-template <bool PHASED>
+// PHASED: x_pad is stored as stride phase planes; SH/SW > 0 give the stride at compile time (the
+// per-store plane arithmetic then uses shifts), 0 reads it from the shape.
+template <bool PHASED, int SH = 0, int SW = 0>
 __global__ void __launch_bounds__(256, 6) conv_repack_kernel(__nv_bfloat16* __restrict__ x_pad, const __nv_bfloat16* __restrict__ src,
                                                           __nv_bfloat16* __restrict__ w_ftc, const __nv_bfloat16* __restrict__ weight,
                                                           ConvTcShape s, int vec_ok, int x_blocks) {
@@ -368,13 +370,14 @@ __global__ void __launch_bounds__(256, 6) conv_repack_kernel(__nv_bfloat16* __re
     const int c0 = static_cast<int>(blockIdx.y) * RP_CH;
     const int nvec = min(RP_CH, s.Cp - c0) / 8;  // 16-byte channel groups this block writes
     const uint4 zero4 = make_uint4(0u, 0u, 0u, 0u);
+    const int xhq_c = conv_tc_xhq(s), xwq_c = conv_tc_xwq(s);
     // Scratch address of padded pixel (hp, wp) of image b, channel c0: one padded image, or (PHASED)
     // position (hp / sh, wp / sw) of phase plane (hp % sh, wp % sw).
     auto px_ptr = [&](int hp, int wp) {
         if constexpr (PHASED) {
-            const int plane = (hp % s.sh) * s.sw + wp % s.sw;
-            const int xhq = conv_tc_xhq(s), xwq = conv_tc_xwq(s);
-            return x_pad + ((static_cast<size_t>(plane) * s.B + b) * xhq + hp / s.sh) * xwq * s.Cp + static_cast<size_t>(wp / s.sw) * s.Cp + c0;
+            const int sh = SH > 0 ? SH : s.sh, sw = SW > 0 ? SW : s.sw;
+            const int plane = (hp % sh) * sw + wp % sw;
+            return x_pad + ((static_cast<size_t>(plane) * s.B + b) * xhq_c + hp / sh) * xwq_c * s.Cp + static_cast<size_t>(wp / sw) * s.Cp + c0;
         } else {
             return x_pad + ((static_cast<size_t>(b) * xhp + hp) * xwp + wp) * s.Cp + c0;
         }
@@ -574,6 +577,8 @@ cudaError_t conv2d_tc_repack(void* scratch, const __nv_bfloat16* input, const __
     dim3 grid(static_cast<unsigned>(x_blocks + w_blocks), (s.Cp + RP_CH - 1) / RP_CH);
     if (s.sh == 1 && s.sw == 1)
         conv_repack_kernel<false><<<grid, 256, 0, stream>>>(x_pad, input, w_ftc, weight, s, vec_ok, static_cast<int>(x_blocks));
+    else if (s.sh == 2 && s.sw == 2)
+        conv_repack_kernel<true, 2, 2><<<grid, 256, 0, stream>>>(x_pad, input, w_ftc, weight, s, vec_ok, static_cast<int>(x_blocks));
     else
         conv_repack_kernel<true><<<grid, 256, 0, stream>>>(x_pad, input, w_ftc, weight, s, vec_ok, static_cast<int>(x_blocks));
     return cudaGetLastError();
