@@ -405,6 +405,41 @@ def test_f32_flash_attention_cuda_cores_vs_oracle(cuda_device, S, D, causal):
     np.testing.assert_allclose(out.cpu().numpy(), expect, **FP32_TOL)
 
 
+@pytest.mark.parametrize("M,K,N,with_bias", [(100, 1000, 70, True),      # K > 512 on a small grid: 32 x 32 x 64 tiles
+                                             (40, 300, 50, False),       # whole-K panels, ragged 16 x 16 tiles
+                                             (1000, 136, 1000, True)])   # 64 x 64 x 16 tiles (256 >= 148 of them)
+def test_f32_matmul_cuda_core_variants_vs_oracle(cuda_device, M, K, N, with_bias):
+    """Each fp32 matmul variant (whole-K panels, 32 x 32 x 64 and 64 x 64 x 16 tiles) against the
+    oracle within the fp32 tolerance."""
+    torch = _torch()
+    rng = np.random.default_rng(M + K + N)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    bias = rng.standard_normal(N, dtype=np.float32) if with_bias else None
+    expect = oracle.matmul(a, b, bias, tiles=(32, 32, 32))
+    out = torch.full((M, N), float("nan"), device=cuda_device)
+    kernels.matmul(out, _to_torch(a, cuda_device), _to_torch(b, cuda_device), None if bias is None else _to_torch(bias, cuda_device))
+    torch.cuda.synchronize()
+    assert runtime.last_kernel() == "matmul_simt_kernel<f32>"
+    np.testing.assert_allclose(out.cpu().numpy(), expect, **FP32_TOL)
+
+
+@pytest.mark.parametrize("x_shape,f,k,stride,pads", [((4, 16, 40, 40), 64, (3, 3), (1, 1), (1, 1, 1, 1)),   # 64 x 32 tiles, 16-deep K steps
+                                                    ((1, 4, 12, 12), 8, (3, 3), (2, 2), (1, 0, 1, 0))])   # K = 36 <= 48
+def test_f32_conv2d_cuda_core_variants_vs_oracle(cuda_device, x_shape, f, k, stride, pads):
+    """The fp32 conv2d kernel's large-grid and shallow-reduction instances against the oracle."""
+    torch = _torch()
+    rng = np.random.default_rng(sum(x_shape) + f)
+    x = rng.uniform(-1, 1, x_shape).astype(np.float32)
+    w = (rng.standard_normal((f, x_shape[1], *k), dtype=np.float32) / np.float32(np.sqrt(x_shape[1] * k[0] * k[1])))
+    expect = oracle.conv2d(x, w, None, stride=stride, dilation=(1, 1), pads=pads, tiles=(8, 16, 4, 8, 9))
+    out = torch.full(expect.shape, float("nan"), device=cuda_device)
+    kernels.conv2d(out, _to_torch(x, cuda_device), _to_torch(w, cuda_device), None, stride, (1, 1), pads)
+    torch.cuda.synchronize()
+    assert runtime.last_kernel() == "conv2d_simt_kernel<f32>"
+    np.testing.assert_allclose(out.cpu().numpy(), expect, **FP32_TOL)
+
+
 def test_c5_full_size_sampled_rows(cuda_device):
     """C5: causal bf16 4x32x8192x128. Sampled (b,h) pairs and query rows vs the oracle (first
     rows, a tile boundary, the last rows: the causal diagonal); every row's output is a convex
