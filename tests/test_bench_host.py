@@ -41,3 +41,18 @@ def test_batch_shards_cover_the_batch_once():
         assert spans[0][0] == 0 and spans[-1][1] == B
         assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
         assert sum(b - a for a, b in spans) == B
+
+
+def test_committed_traffic_matches_the_kernel_labels_the_bench_reports():
+    """roofline.traffic comes from profiles/traffic.json under "<kernel label>/<config>": every
+    label the tensor-core configurations report today has its ncu figure."""
+    for label, config in (("gemm_bf16_tc_pair_kernel<512>", "C4"), ("flash_fwd_tc_kernel", "C5"), ("conv2d_tc_kernel", "X1")):
+        traffic = bench.load_traffic(label, config)
+        assert isinstance(traffic, int) and traffic > 0, (label, config)
+    assert bench.load_traffic("no_such_kernel", "C4") is None
+
+
+def test_launch_count_per_step_follows_the_kernel():
+    assert bench.launches_per_step("conv2d_tc_kernel") == 2  # repack + conv
+    for label in ("gemm_bf16_tc_pair_kernel<512>", "gemm_bf16_tc_pair_kernel<256>", "flash_fwd_tc_kernel", "matmul_simt_kernel<f32>"):
+        assert bench.launches_per_step(label) == 1
