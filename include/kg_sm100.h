@@ -133,7 +133,12 @@ KG_API int kg_sm100_matmul(float* out, const void* lhs, const void* rhs, int in_
 
 /* NCHW conv2d: out[B,F,HO,WO] (f32) with HO = (XH+pt+pb-dh*(KH-1)-1)/sh+1, WO likewise. bf16 runs
  * on tcgen05 tensor cores for any stride and dilation (a repack into device scratch first), f32 on
- * exact FFMA. */
+ * exact FFMA.
+ * The bf16 repack scratch is ONE buffer per device, shared by every call in the process: calls
+ * that may overlap on the GPU (on different streams, or from different host threads) race on it,
+ * so order them on one stream or with events. The first call on a device, and any call that needs
+ * more scratch than every earlier one, synchronises the device and calls cudaMalloc; make such a
+ * call once before capturing a stream into a CUDA graph. */
 KG_API int kg_sm100_conv2d(float* out, const void* input, const void* weight, int in_dtype, const float* bias,
                     long long B, long long C, long long XH, long long XW, long long F, long long KH, long long KW,
                     long long stride_h, long long stride_w, long long dilation_h, long long dilation_w,
@@ -154,9 +159,12 @@ KG_API int kg_sm100_flash_attention(void* out, const void* q, const void* k, con
  * cudaMalloc, cudaFree or other allocating routine is called.
  *  - The first call on each device looks up the array's device address (with that device
  *    current); make that first call before any stream capture.
- *  - Inputs needing more scratch than the array holds (B*XH*XW*Cp*2 rounded up to 256 bytes plus
- *    F*KH*KW*Cp*2, Cp = C rounded up to a multiple of 8), f32 inputs and strides other than 1
- *    return KG_ERR_UNSUPPORTED with a message.
+ *  - Scratch needed: round256(B * (XH+pt+pb) * XWq * Cp * 2) + F * KH * KW * Cp * 2 bytes, where
+ *    Cp = C rounded up to a multiple of 8 and XWq = XW+pl+pr, rounded up to a multiple of 4 when
+ *    WO is one. When KW * Cp <= 64 (few channels) the KW horizontal taps are folded into the
+ *    channels: Cp becomes KW * Cp and KW becomes 1 in the formula. Inputs needing more than the
+ *    array holds, f32 inputs and strides other than 1 return KG_ERR_UNSUPPORTED with a message
+ *    that gives the exact byte count.
  *  - All calls share the array; each call rewrites every element it reads, so nothing left by a
  *    previous call leaks into a result, but calls that overlap on the GPU (other streams, other
  *    host threads) race on it: order them on one stream. */

@@ -16,6 +16,7 @@
 
 #include "../../include/kg_sm100.h"
 #include "kg_conv_tc.h"
+#include "kg_device_once.h"
 #include "kg_flash_tc.h"
 #include "kg_gemm_tc.h"
 #include "kg_simt.h"
@@ -55,18 +56,24 @@ struct DeviceInfo {
     int* status = nullptr;  // device address of kg_device_status_word
 };
 
+// Per-device state lives in fixed arrays indexed by the device ordinal, so a pointer handed out
+// under g_mu stays valid after the lock is released, whatever other threads do meanwhile.
 std::mutex g_mu;
-std::vector<DeviceInfo> g_devices;
+DeviceInfo g_devices[kg::kMaxDevices];
 // Slot entries are synchronous and share one staging arena per device: one call at a time.
 std::mutex g_call_mu;
 
+int current_device(int* dev) {
+    KG_CUDA_TRY(cudaGetDevice(dev));
+    if (*dev < 0 || *dev >= kg::kMaxDevices) return fail(KG_ERR_UNSUPPORTED, "device ordinal %d beyond the %d this library tracks", *dev, kg::kMaxDevices);
+    return KG_OK;
+}
+
 int device_info(DeviceInfo** out) {
     int dev = 0;
-    KG_CUDA_TRY(cudaGetDevice(&dev));
+    int rc = current_device(&dev);
+    if (rc != KG_OK) return rc;
     std::lock_guard<std::mutex> lock(g_mu);
-    if (static_cast<int>(g_devices.size()) <= dev) {
-        g_devices.resize(dev + 1);
-    }
     DeviceInfo& info = g_devices[dev];
     if (info.num_sms == 0) {
         KG_CUDA_TRY(cudaDeviceGetAttribute(&info.num_sms, cudaDevAttrMultiProcessorCount, dev));
@@ -156,13 +163,13 @@ struct Scratch {
     void* ptr = nullptr;
     size_t cap = 0;
 };
-std::vector<Scratch> g_scratch;
+Scratch g_scratch[kg::kMaxDevices];
 
 int device_scratch(size_t bytes, void** out) {
     int dev = 0;
-    KG_CUDA_TRY(cudaGetDevice(&dev));
+    int rc = current_device(&dev);
+    if (rc != KG_OK) return rc;
     std::lock_guard<std::mutex> lock(g_mu);
-    if (static_cast<int>(g_scratch.size()) <= dev) g_scratch.resize(dev + 1);
     Scratch& sc = g_scratch[dev];
     if (sc.cap < bytes) {
         // The previous buffer may still be read by kernels in flight on any stream.
@@ -475,7 +482,7 @@ struct Staging {
     void* ptr = nullptr;
     size_t cap = 0;
 };
-std::vector<Staging> g_staging;
+Staging g_staging[kg::kMaxDevices];
 
 // Host-memory arguments get device copies in a per-device staging arena (`stage_alloc` assigns
 // them device space; nothing is copied).
@@ -495,9 +502,9 @@ int stage_alloc(std::vector<MemArg*>& args) {
     }
     if (total == 0) return KG_OK;
     int dev = 0;
-    KG_CUDA_TRY(cudaGetDevice(&dev));
+    int rc = current_device(&dev);
+    if (rc != KG_OK) return rc;
     std::lock_guard<std::mutex> lock(g_mu);
-    if (static_cast<int>(g_staging.size()) <= dev) g_staging.resize(dev + 1);
     Staging& st = g_staging[dev];
     if (st.cap < total) {
         if (st.ptr) KG_CUDA_TRY(cudaFree(st.ptr));
@@ -525,13 +532,13 @@ struct Pipe {
     cudaEvent_t computed[kPipeMaxChunks] = {};
     cudaEvent_t operands = nullptr;
 };
-std::vector<Pipe> g_pipes;
+Pipe g_pipes[kg::kMaxDevices];
 
 int get_pipe(Pipe** out) {
     int dev = 0;
-    KG_CUDA_TRY(cudaGetDevice(&dev));
+    int rc = current_device(&dev);
+    if (rc != KG_OK) return rc;
     std::lock_guard<std::mutex> lock(g_mu);
-    if (static_cast<int>(g_pipes.size()) <= dev) g_pipes.resize(dev + 1);
     Pipe& p = g_pipes[dev];
     if (p.up == nullptr) {
         KG_CUDA_TRY(cudaStreamCreateWithFlags(&p.up, cudaStreamNonBlocking));

@@ -24,6 +24,7 @@
 // Warps per CTA: 0 TMA producer, 1 MMA issuer (even CTA), 2..9 epilogue (the epilogue is as long as
 // a tile's MMAs, so it gets two warps per TMEM lane quarter).
 #include "kg_conv_tc.h"
+#include "kg_device_once.h"
 #include "kg_ptx.cuh"
 
 namespace kg {
@@ -242,7 +243,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const size_t plane = static_cast<size_t>(s.HO) * s.WO;
         uint32_t acc = 0, acc_phase = 0, epi_phase = 0;
         bool alive = true;
-        for (int tile = tile_begin; tile < tile_end && alive && !*abort; ++tile) {
+        for (int tile = tile_begin; tile < tile_end && alive && !warp_aborted(abort); ++tile) {
             int mb, nb;
             conv_tile_coords(tile, num_m, num_n, mb, nb);
             // this lane's 4 pixels (store phase): padded pixel -> (b, ho, wo); rows outside the output are dropped
@@ -260,7 +261,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                 if (p < rows && ho < s.HO && wo < s.WO) valid |= 1u << i;
             }
             const bool vec = vec_ok && valid == 0xFu;
-            if (!mbar_wait_cluster(&bars->tfull[acc], acc_phase, abort, status, kDevTimeoutEpilogue)) break;
+            if (!warp_all(mbar_wait_cluster(&bars->tfull[acc], acc_phase, abort, status, kDevTimeoutEpilogue))) break;
             tc_fence_after();
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * PBN;
 #pragma unroll 1
@@ -277,7 +278,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < 16; ++j) buf[(half * 16 + j) * 128 + quarter * 32 + lane] = __uint_as_float(r[j]);
                 mbar_arrive(&bars->epi);
-                if (!mbar_wait(&bars->epi, epi_phase, abort, status, kDevTimeoutEpilogue)) {
+                if (!warp_all(mbar_wait(&bars->epi, epi_phase, abort, status, kDevTimeoutEpilogue))) {
                     alive = false;
                     break;
                 }
@@ -501,15 +502,11 @@ cudaError_t launch_pbn(const CUtensorMap& tm_x, const CUtensorMap& tm_w, float* 
                        int* status, cudaStream_t stream) {
     constexpr size_t smem = conv_smem_bytes<PBN>();
     static_assert(smem <= 227 * 1024, "shared memory");
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    static DeviceOnce attr_once;  // the shared-memory opt-in is a per-device function attribute
+    cudaError_t e = attr_once.run([] {
+        return cudaFuncSetAttribute(conv2d_tc_kernel<PBN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    });
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(conv2d_tc_kernel<PBN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
     const long long num_tiles = ((conv_tc_rows(s) + PBM - 1) / PBM) * ((s.F + PBN - 1) / PBN);
     const long long max_pairs = num_sms / 2 > 0 ? num_sms / 2 : 1;
     const int pairs = static_cast<int>(num_tiles < max_pairs ? num_tiles : max_pairs);

@@ -20,6 +20,7 @@
 // The running max is only moved when it grows by more than 2^8 (log2 domain); O and l keep using
 // the stale max otherwise, which is exact because both are scaled by the same factor.
 #include "kg_flash_tc.h"
+#include "kg_device_once.h"
 #include "kg_ptx.cuh"
 
 namespace kg {
@@ -319,7 +320,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         float l_run = 0.0f;
         const int n = n_tiles(i);
         for (int j = 0; j < n; ++j) {
-            if (!mbar_wait(&bars->s_ready[i], j & 1u, abort, status, kDevTimeoutSoftmax)) break;
+            if (!warp_all(mbar_wait(&bars->s_ready[i], j & 1u, abort, status, kDevTimeoutSoftmax))) break;
             tc_fence_after();
             // Scores of this row: 128 f32 in registers.
             // All four TMEM loads are in flight before the single wait.
@@ -410,8 +411,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             l_run = l_run * alpha + (sum_lo + sum_hi);
         }
         // epilogue: O / l -> bf16 -> global
-        if (n > 0 && !*abort) {
-            if (mbar_wait(&bars->o_done[i], 0, abort, status, kDevTimeoutEpilogue)) {
+        if (n > 0 && !warp_aborted(abort)) {
+            if (warp_all(mbar_wait(&bars->o_done[i], 0, abort, status, kDevTimeoutEpilogue))) {
                 tc_fence_after();
                 const float inv = 1.0f / l_run;
                 __nv_bfloat16* dst = out + (static_cast<size_t>(bh) * S + row) * D;
@@ -460,6 +461,19 @@ static int flash_group_heads(int BH, int S, int D) {
     return g;
 }
 
+// Per-device set-up of flash_fwd_tc_kernel<D>: the shared-memory opt-in, and a check of the
+// compiled register count. The warpgroups' setmaxnreg budgets assume LAUNCH_REGS registers per
+// thread at launch; with fewer, the softmax warpgroups' increase could never be granted, so the
+// launch is refused.
+template <int D>
+static cudaError_t flash_fwd_tc_setup() {
+    cudaError_t e = cudaFuncSetAttribute(flash_fwd_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FlashCfg<D>::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    cudaFuncAttributes fa{};
+    if ((e = cudaFuncGetAttributes(&fa, flash_fwd_tc_kernel<D>)) != cudaSuccess) return e;
+    return fa.numRegs == LAUNCH_REGS ? cudaSuccess : cudaErrorInvalidConfiguration;
+}
+
 size_t flash_fwd_tc_smem_bytes(int D) { return D == 64 ? FlashCfg<64>::SMEM_BYTES : FlashCfg<128>::SMEM_BYTES; }
 
 cudaError_t flash_fwd_tc_launch(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v, __nv_bfloat16* out,
@@ -468,25 +482,9 @@ cudaError_t flash_fwd_tc_launch(const CUtensorMap& tm_q, const CUtensorMap& tm_k
     const float scale_log2 = scale * 1.4426950408889634f;
     const int group_heads = flash_group_heads(BH, S, D);
     dim3 grid(static_cast<unsigned>(num_pairs) * static_cast<unsigned>(BH));
-    static bool attr_set[2][64] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    static DeviceOnce attr_once[2];
+    const cudaError_t e = D == 64 ? attr_once[0].run(flash_fwd_tc_setup<64>) : attr_once[1].run(flash_fwd_tc_setup<128>);
     if (e != cudaSuccess) return e;
-    const int which = D == 64 ? 0 : 1;
-    if (dev < 0 || dev >= 64 || !attr_set[which][dev]) {
-        e = D == 64 ? cudaFuncSetAttribute(flash_fwd_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)FlashCfg<64>::SMEM_BYTES)
-                    : cudaFuncSetAttribute(flash_fwd_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)FlashCfg<128>::SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        // The warpgroups' setmaxnreg budgets assume LAUNCH_REGS registers per thread at launch; with
-        // fewer, the softmax warpgroups' increase could never be granted, so refuse to launch.
-        cudaFuncAttributes fa{};
-        e = D == 64 ? cudaFuncGetAttributes(&fa, flash_fwd_tc_kernel<64>) : cudaFuncGetAttributes(&fa, flash_fwd_tc_kernel<128>);
-        if (e != cudaSuccess) return e;
-        if (fa.numRegs != LAUNCH_REGS) return cudaErrorInvalidConfiguration;
-        if (dev >= 0 && dev < 64) attr_set[which][dev] = true;
-    }
     if (D == 64) {
         flash_fwd_tc_kernel<64><<<grid, NUM_THREADS, FlashCfg<64>::SMEM_BYTES, stream>>>(tm_q, tm_k, tm_v, out, S, scale_log2, causal,
                                                                                          num_pairs, BH, group_heads, status);

@@ -13,6 +13,7 @@
 //               accumulator is released as soon as it has been read so the next tile's MMAs overlap.
 // Tiles are visited in a grouped raster (GROUP_M m-blocks at a time) for L2 reuse of both operands.
 #include "kg_gemm_tc.h"
+#include "kg_device_once.h"
 #include "kg_ptx.cuh"
 
 namespace kg {
@@ -201,10 +202,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int quarter = warp & 3;  // TMEM lane quarter this warp may access
         const int row_in_tile = quarter * 32 + lane;
         uint32_t acc = 0, acc_phase = 0;
-        for (int tile = blockIdx.x; tile < num_tiles && !*abort; tile += gridDim.x) {
+        for (int tile = blockIdx.x; tile < num_tiles && !warp_aborted(abort); tile += gridDim.x) {
             int mb, nb;
             tile_coords(tile, num_m, num_n, mb, nb);
-            if (!mbar_wait(&bars->tfull[acc], acc_phase, abort, status, kDevTimeoutEpilogue)) {
+            if (!warp_all(mbar_wait(&bars->tfull[acc], acc_phase, abort, status, kDevTimeoutEpilogue))) {
                 break;
             }
             tc_fence_after();
@@ -283,21 +284,11 @@ cudaError_t gemm_bf16_tc_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_b
     const int vec_ok = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
                        (bias == nullptr || (reinterpret_cast<uintptr_t>(bias) & 15u) == 0);
     // The shared-memory opt-in is a per-device function attribute: set it once per device.
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) {
-        return e;
-    }
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-        if (e != cudaSuccess) {
-            return e;
-        }
-        if (dev >= 0 && dev < 64) {
-            attr_set[dev] = true;
-        }
-    }
+    static DeviceOnce attr_once;
+    const cudaError_t e = attr_once.run([] {
+        return cudaFuncSetAttribute(gemm_bf16_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    });
+    if (e != cudaSuccess) return e;
     const int num_tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
     const int grid = num_tiles < num_sms ? num_tiles : num_sms;
     gemm_bf16_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(tm_a, tm_b, out, bias, M, N, K, vec_ok, status);

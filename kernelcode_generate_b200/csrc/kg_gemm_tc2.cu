@@ -18,6 +18,7 @@
 // power, so under the 1 kW cap the SMs hold a higher clock; the price is a single accumulator, so
 // each tile's epilogue is not overlapped with MMAs. gemm_bf16_tc_pair_block_n picks the width.
 #include "kg_gemm_tc.h"
+#include "kg_device_once.h"
 #include "kg_ptx.cuh"
 
 namespace kg {
@@ -225,10 +226,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         uint32_t chunk_count = 0;
         const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&bars->tempty[0]), 0), mapa_shared(smem_u32(&bars->tempty[1]), 0)};
         uint32_t acc = 0, acc_phase = 0;
-        for (int tile = pair; tile < num_tiles && !*abort; tile += num_pairs) {
+        for (int tile = pair; tile < num_tiles && !warp_aborted(abort); tile += num_pairs) {
             int mb, nb;
             pair_tile_coords(tile, num_m, num_n, mb, nb);
-            if (!mbar_wait_cluster(&bars->tfull[acc], acc_phase, abort, status, kDevTimeoutEpilogue)) break;
+            if (!warp_all(mbar_wait_cluster(&bars->tfull[acc], acc_phase, abort, status, kDevTimeoutEpilogue))) break;
             tc_fence_after();
             const int row = mb * PBM + static_cast<int>(rank) * 128 + quarter * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * PBN;
@@ -338,15 +339,11 @@ static cudaError_t launch_pbn(const CUtensorMap& tm_a, const CUtensorMap& tm_b, 
     static_assert(SMEM_BYTES <= 227 * 1024, "shared memory");
     const int vec_ok = (N % 4) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0 &&
                        (bias == nullptr || (reinterpret_cast<uintptr_t>(bias) & 15u) == 0);
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    static DeviceOnce attr_once;  // the shared-memory opt-in is a per-device function attribute
+    const cudaError_t e = attr_once.run([] {
+        return cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<PBN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
+    });
     if (e != cudaSuccess) return e;
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-        e = cudaFuncSetAttribute(gemm_bf16_tc_pair_kernel<PBN>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        if (dev >= 0 && dev < 64) attr_set[dev] = true;
-    }
     const int num_tiles = ((M + PBM - 1) / PBM) * ((N + PBN - 1) / PBN);
     const int max_pairs = num_sms / 2;
     const int pairs = num_tiles < max_pairs ? num_tiles : max_pairs;

@@ -102,6 +102,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     return mbar_wait_for(bar, parity, abort, status, err, KG_WAIT_TIMEOUT_NS);
 }
 
+// Roles whose 32 lanes all wait and then run .sync.aligned instructions (tcgen05.ld / tcgen05.st)
+// must take every branch together. Each lane polls a barrier on its own, so near a deadline, or
+// when another role raises the abort flag, one lane could give up while its neighbours go on into
+// an aligned instruction without it, which is undefined. These votes make the whole warp go on or
+// the whole warp give up; every lane of the warp must execute them.
+__device__ __forceinline__ bool warp_all(bool ok) { return __all_sync(0xffffffffu, ok); }
+__device__ __forceinline__ bool warp_aborted(const volatile int* abort) { return __any_sync(0xffffffffu, *abort != 0); }
+
 // ---------------------------------------------------------------- TMA (no multicast)
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

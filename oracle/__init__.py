@@ -26,7 +26,17 @@ ORACLE_DIR = Path(__file__).resolve().parent
 PORT_LIB = ORACLE_DIR / "_build" / "libkg_oracle.so"
 REF_LIB_O0 = ORACLE_DIR / "_ref" / "libkg_ref_O0.so"
 REF_LIB_O2 = ORACLE_DIR / "_ref" / "libkg_ref_O2.so"
-DEFAULT_REFERENCE_ROOT = Path(os.environ.get("KG_REFERENCE_ROOT", "/root/reference"))
+
+
+def reference_root() -> Path | None:
+    """The reference checkout (violetDelia/kernelcode_generate) whose npu_demo headers the harness
+    compiles against: $KG_REFERENCE_ROOT when set, else a checkout named ``reference`` beside this
+    repository. None when neither holds the reference's ``include/npu_demo/npu_demo.h``."""
+    env = os.environ.get("KG_REFERENCE_ROOT")
+    for cand in ([Path(env)] if env else []) + [ORACLE_DIR.parent.parent / "reference"]:
+        if (cand / "include" / "npu_demo" / "npu_demo.h").exists():
+            return cand.resolve()
+    return None
 
 F32 = 1
 BF16 = 5
@@ -46,10 +56,12 @@ def build_port() -> Path:
     return PORT_LIB
 
 
-def build_ref(reference_root: Path | None = None) -> bool:
-    """Compile ref_harness.cpp against the reference's npu_demo headers, when present."""
-    root = Path(reference_root or DEFAULT_REFERENCE_ROOT)
-    if not (root / "include" / "npu_demo" / "npu_demo.h").exists():
+def build_ref(root: Path | None = None) -> bool:
+    """Compile ref_harness.cpp against the reference's npu_demo headers, when the reference
+    checkout is present (``root``, else ``reference_root()``); otherwise keep the libraries already
+    built. Returns whether both libraries exist."""
+    root = Path(root) if root is not None else reference_root()
+    if root is None or not (root / "include" / "npu_demo" / "npu_demo.h").exists():
         return REF_LIB_O2.exists() and REF_LIB_O0.exists()
     subprocess.run(["make", "-s", "-C", str(ORACLE_DIR), "ref", f"REF_ROOT={root}"], check=True)
     return True

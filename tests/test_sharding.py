@@ -138,3 +138,48 @@ def test_gather_rows_assembles_the_single_process_result(world):
     q, k, v = (rng.standard_normal((2, 3, 40, 16), dtype=np.float32) for _ in range(3))
     np.testing.assert_array_equal(att, oracle.flash_attention(q, k, v, tiles=(16, 16), scale=0.25, causal=True).reshape(6, 40, 16))
     assert bad is not None and "block" in bad
+
+
+def _replicate_worker(rank, world, port, results):
+    import torch
+    import torch.distributed as dist
+
+    from kernelcode_generate_b200.sharding import replicate_from_host_shards, shard_range
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rng = np.random.default_rng(21)
+        b = torch.from_numpy(rng.standard_normal((37, 19), dtype=np.float32))
+        # Each rank holds only its own rows of B; the rest of its host copy is garbage that must
+        # never reach the replica.
+        k0, k1 = shard_range(37, rank, world)
+        host = torch.full_like(b, float("nan"))
+        host[k0:k1] = b[k0:k1]
+        first = replicate_from_host_shards(host, torch.device("cpu")).clone()
+        second = replicate_from_host_shards(host * 2, torch.device("cpu")).clone()  # buffers reused
+        results.put((rank, first.numpy(), second.numpy()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_b_is_replicated_from_one_upload_per_row_block(world):
+    """The multi-GPU host-buffer matmul uploads each row of B from one rank only and all-gathers
+    it: every rank ends with the whole B, bit for bit, from host copies that hold only its own
+    rows (37 rows: uneven blocks over 2 and 3 ranks), and a second call reuses the buffers."""
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_replicate_worker, args=(r, world, port, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [results.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    b = np.random.default_rng(21).standard_normal((37, 19), dtype=np.float32)
+    for _, first, second in got:
+        np.testing.assert_array_equal(first, b)
+        np.testing.assert_array_equal(second, 2 * b)
