@@ -63,6 +63,8 @@ def parse_args(argv=None):
                     help="at N > 1, skip the NCCL all-gather of the sharded output after the timed loop")
     ap.add_argument("--sustained-seconds", type=float, default=2.5,
                     help="length of the back-to-back run of the headline kernel (0 skips it)")
+    ap.add_argument("--shard-of", type=int, default=None,
+                    help="on one GPU, run rank 0's shard of a job with this many ranks (to time or profile one rank's launch)")
     return ap.parse_args(argv)
 
 
@@ -653,7 +655,9 @@ def main(argv=None):
     peaks, peak_src = load_peaks()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
     cfg = workloads.ALL_CONFIGS[args.config]
-    wl = Workload(cfg, rank, world, dev)
+    if args.shard_of is not None and (world != 1 or args.shard_of < 1):
+        raise SystemExit("--shard-of runs one rank's shard on one GPU: use it without torchrun, with a positive rank count")
+    wl = Workload(cfg, 0, args.shard_of, dev) if args.shard_of else Workload(cfg, rank, world, dev)
     with ClockSampler(local) as clocks:
         job_ms, launch_ms, kernel = time_steps(wl, args.steps, args.warmup, world, flush)
     total_flops = job_flops(float(wl.flops), cfg, world)
@@ -705,7 +709,7 @@ def main(argv=None):
             "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(job_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": cfg.dtype, "data": "synthetic",
-            "config": workload_config(cfg, world),
+            "config": {**workload_config(cfg, world), **({"shard_of": args.shard_of} if args.shard_of else {})},
             "frac_of_peak": round(value / (tensor_peak * gpus), 4),
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": tensor_peak, "unit": "TFLOP/s",
                          "frac": round(achieved / tensor_peak, 4), "traffic": traffic, "kernel": kernel,
