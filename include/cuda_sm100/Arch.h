@@ -33,6 +33,10 @@ __device__ inline S_INT thread_id() {
     return static_cast<S_INT>(threadIdx.x) + static_cast<S_INT>(blockDim.x) * (threadIdx.y + static_cast<S_INT>(blockDim.y) * threadIdx.z);
 }
 __device__ inline S_INT thread_num() { return static_cast<S_INT>(blockDim.x) * blockDim.y * blockDim.z; }
+// No sub-thread level on this target (launch<> requires subthread == 1): every thread is its own
+// single sub-thread.
+__device__ inline S_INT subthread_id() { return 0; }
+__device__ inline S_INT subthread_num() { return 1; }
 __device__ inline void barrier() { __syncthreads(); }
 
 __device__ inline unsigned dynamic_smem_bytes() {

@@ -12,11 +12,13 @@ unchanged with ``target="cuda_sm100"``:
 
 What differs, by design:
 
-* ``compile`` does not run a compiler. The sm_100a kernels are built ahead of time (nvcc
-  ``-gencode arch=compute_100a,code=sm_100a``); ``function`` (the DSL wrapper name) selects the
-  compiled-kernel shim ``libkg_sm100_<kernel>.so`` whose ``kg_execute_entry`` takes the same
-  argument slots as the reference's generated entry. ``source``, when given, is recorded on the
-  ``CompiledKernel`` (an IR-level emitter for this target is not part of this backend).
+* ``compile`` goes through the target's compile strategy (``cuda_sm100_strategy``). For the DSL
+  wrappers of the three benchmarked kernels it runs no compiler: the fused sm_100a kernels are
+  built ahead of time (nvcc ``-gencode arch=compute_100a,code=sm_100a``) and ``function``
+  selects the compiled-kernel shim ``libkg_sm100_<kernel>.so``, whose ``kg_execute_entry`` takes
+  the same argument slots as the reference's generated entry (``source``, when given, is
+  recorded). Any other ``function`` needs a generated ``source`` on the ``include/cuda_sm100``
+  surface defining ``kg_execute_entry``, which the strategy builds with nvcc for sm_100a.
 * Memory arguments may be torch CUDA tensors (device pointers, no copies) as well as numpy
   arrays / CPU tensors (staged through device memory inside the call).
 * bf16 memory (torch.bfloat16) is accepted with dtype code 5; the reference has no bf16 code.
@@ -220,15 +222,23 @@ class CompiledKernel:
     compile_stdout: str = ""
     compile_stderr: str = ""
     source: str | None = field(default=None, repr=False, compare=False)
+    allow_absent_memory_args: tuple[tuple[int, str, int], ...] = field(default=(), repr=False, compare=False)
+    cleanup: Callable[[], None] | None = field(default=None, repr=False, compare=False)
     _closed: list = field(default_factory=lambda: [False], repr=False, compare=False)
 
     @property
-    def spec(self) -> _KernelSpec:
-        return KERNELS[self.function]
+    def spec(self) -> _KernelSpec | None:
+        """The prebuilt kernel's argument contract, or None for a kernel built from a generated source."""
+        return KERNELS.get(self.function)
 
     def close(self) -> None:
-        """Idempotent; the shim library stays loaded for other kernels of the process."""
+        """Idempotent. A prebuilt shim stays loaded for other kernels of the process; a kernel built
+        from a generated source has its work directory removed."""
+        if self._closed[0]:
+            return
         self._closed[0] = True
+        if self.cleanup is not None:
+            self.cleanup()
 
     def execute(self, args: tuple | None = None, *, request: ExecuteRequest | None = None, entry_point: str | None = None,
                 capture_function_output: bool = False, stream: Any = None) -> ExecuteResult:
@@ -254,12 +264,17 @@ class CompiledKernel:
         if resolved != self.entry_point:
             raise KernelCodeError(_SYMBOL_RESOLVE_FAILED, "entry_point mismatch")
         spec = self.spec
-        if len(args) not in spec.arg_count:
-            raise KernelCodeError(_RUNTIME_THROW_OR_ABORT, f"{self.function} takes {spec.arg_count} args, got {len(args)}")
-        slot_args = spec.expand(args) if spec.expand else args
-        if stream is not None:
-            return self._execute_on_stream(spec, slot_args, stream)
-        slots, keep = marshal_slots(slot_args, spec.absent_memory_args)
+        if spec is None:  # built from a generated source: its own slot contract, synchronous only
+            if stream is not None:
+                raise KernelCodeError(_STREAM_NOT_SUPPORTED, "a kernel built from a generated source runs synchronously: stream must be None")
+            slot_args, absent = args, self.allow_absent_memory_args
+        else:
+            if len(args) not in spec.arg_count:
+                raise KernelCodeError(_RUNTIME_THROW_OR_ABORT, f"{self.function} takes {spec.arg_count} args, got {len(args)}")
+            slot_args, absent = (spec.expand(args) if spec.expand else args), spec.absent_memory_args
+            if stream is not None:
+                return self._execute_on_stream(spec, slot_args, stream)
+        slots, keep = marshal_slots(slot_args, absent)
         if capture_function_output:
             return self._execute_capture(slots, keep, len(slot_args), resolved)
         entry = _load_entry(self.soname_path, resolved)
@@ -387,14 +402,12 @@ class ExecutionEngine:
             raise KernelCodeError(_SOURCE_EMPTY_OR_INVALID, "function must be a non-empty wrapper name")
         if request.source is not None and (not isinstance(request.source, str) or not request.source.strip()):
             raise KernelCodeError(_SOURCE_EMPTY_OR_INVALID, "source is empty")
-        spec = KERNELS.get(request.function)
-        if spec is None:
-            raise KernelCodeError(_COMPILE_FAILED, f"no sm_100a kernel for wrapper {request.function!r}; served: {sorted(KERNELS)}")
-        shim = runtime.SHIM_PATHS[spec.kernel]
-        if not shim.exists():
-            raise KernelCodeError(_COMPILE_FAILED, f"{shim} is not built; run `python -m kernelcode_generate_b200._build`")
-        return CompiledKernel(target=request.target, soname_path=str(shim), function=request.function,
-                              entry_point=request.entry_point, source=request.source)
+        if request.function not in KERNELS and request.source is None:
+            raise KernelCodeError(_COMPILE_FAILED, f"no sm_100a kernel for wrapper {request.function!r} and no source to build; "
+                                                   f"prebuilt: {sorted(KERNELS)}")
+        from .cuda_sm100_strategy import CudaSm100CompileStrategy
+
+        return CudaSm100CompileStrategy().compile(request)
 
 
 __all__ = ["CompileRequest", "CompiledKernel", "ExecuteRequest", "ExecuteResult", "ExecutionEngine", "KernelCodeError",

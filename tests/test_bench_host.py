@@ -73,6 +73,19 @@ def test_a_shard_never_reports_the_full_problem_traffic():
     assert bench.launch_shape(c5, bench.shard_range(128, 3, 8)) == "BH16_S8192_D128_causal"
 
 
+def test_every_shard_launch_of_the_scaling_run_has_its_own_capture():
+    """The N = 2 / 4 / 8 launches each have a capture of their own shape (the tile width the
+    library picks: 256 columns for 4096 rows, 512 for 2048 and 1024 rows), smaller than the full
+    problem's, and C5's 16-plane shard at N = 8 too."""
+    c4, c5 = workloads.ALL_CONFIGS["C4"], workloads.ALL_CONFIGS["C5"]
+    full = bench.load_traffic("gemm_bf16_tc_pair_kernel<512>", "M8192_N8192_K8192")
+    for world, label in ((2, "gemm_bf16_tc_pair_kernel<256>"), (4, "gemm_bf16_tc_pair_kernel<512>"), (8, "gemm_bf16_tc_pair_kernel<512>")):
+        t = bench.load_traffic(label, bench.launch_shape(c4, bench.shard_range(8192, 0, world)))
+        assert isinstance(t, int) and 0 < t < full, (world, t)
+    t5 = bench.load_traffic("flash_fwd_tc_kernel", bench.launch_shape(c5, bench.shard_range(128, 0, 8)))
+    assert isinstance(t5, int) and 0 < t5 < bench.load_traffic("flash_fwd_tc_kernel", "BH128_S8192_D128_causal")
+
+
 def test_replicated_configurations_count_one_replica():
     """C2 (batch 1) cannot be split: at N > 1 every rank computes the same problem, and the job's
     work is one replica's, not N times it; sharded configurations sum their shards."""
