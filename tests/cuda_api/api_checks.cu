@@ -227,6 +227,130 @@ __global__ void matmul_nest_kernel(float* out_p, const float* lhs_p, const float
     if (rc != 0 && thread_id() == 0) atomicExch(status, 1);
 }
 
+// ---------------------------------------------------------------- rings and tile allocation
+// The reference's known answers for dma.make_ring / current / advance
+// (test/include/api/test_dma.py:225-297) and dma.alloc (test_dma.py:653-700), on a thread block.
+__global__ void ring_alloc_kat_kernel(int* codes) {
+    DevCtx ctx;
+    __shared__ __align__(16) int8_t backing_data[64];
+    __shared__ __align__(16) int8_t small_data[40];
+    if (thread_id() < 64) backing_data[thread_id()] = 0;
+    barrier();
+    Memory<TLM1, int8_t> backing(backing_data, {64}, {1});
+    auto ring = make_ring<float>(backing, 2, 32, {2, 3}, {4, 1});
+    Memory<TLM1, float> cur0 = ring.current();
+    CHECK(1, ring.valid() && cur0.data() == reinterpret_cast<float*>(backing_data));
+    CHECK(2, cur0.rank() == 2 && cur0.get_shape(0) == 2 && cur0.get_shape(1) == 3);
+    CHECK(3, cur0.get_stride(0) == 4 && cur0.get_stride(1) == 1);
+    CHECK(4, ring.current().data() == cur0.data());  // current() does not move the cursor
+    Memory<TLM1, float> cur1 = ring.advance();
+    CHECK(5, reinterpret_cast<int8_t*>(cur1.data()) == backing_data + 32);  // byte offsets, not element offsets
+    CHECK(6, ring.current().data() == cur1.data());
+    CHECK(7, ring.advance().data() == cur0.data());  // wraps after num slots
+    CHECK(8, !make_ring<float>(backing, 0, 32, {2, 3}, {4, 1}).valid());   // num must be positive
+    CHECK(9, !make_ring<float>(backing, 2, 16, {2, 3}, {4, 1}).valid());   // a 28-byte slot does not fit 16 bytes
+    Memory<TLM1, int8_t> small(small_data, {40}, {1});
+    CHECK(10, !make_ring<float>(small, 2, 32, {2, 3}, {4, 1}).valid());    // 2 x 32 bytes exceed 40
+    CHECK(11, !make_ring<float>(backing, 2, 32, {2, 3}, {4}).valid());     // shape and stride ranks differ
+    auto one = make_ring<float>(backing, 1, 32, {2, 3}, {4, 1});
+    CHECK(12, one.valid() && one.advance().data() == one.current().data() && one.cursor() == 0);  // one slot: advance stays
+    auto invalid = make_ring<float>(backing, 2, 0, {2, 3}, {4, 1});
+    CHECK(13, !invalid.valid() && !invalid.current().valid() && !invalid.advance().valid());
+    // slot order over seven advances of a 3-slot ring: cursor 1, 2, 0, 1, 2, 0, 1
+    auto r3 = make_ring<float>(backing, 3, 16, {2}, {1});
+    bool order_ok = r3.cursor() == 0;
+    for (int i = 1; i <= 7; ++i) {
+        Memory<TLM1, float> slot = r3.advance();
+        order_ok = order_ok && r3.cursor() == i % 3 && reinterpret_cast<int8_t*>(slot.data()) == backing_data + 16 * (i % 3);
+    }
+    CHECK(14, order_ok);
+    // a ring's slot is an ordinary Memory: helpers work on it
+    Memory<TLM1, float> slot0 = ring.current();
+    CHECK(15, fill<TLM1, float>(ctx, slot0, 1.5f) == kOk && reinterpret_cast<float*>(backing_data)[4] == 1.5f &&
+              reinterpret_cast<float*>(backing_data)[3] != 1.5f);  // element (1, 0) at offset 4; offset 3 lies between rows
+    barrier();
+    // alloc from the block's dynamic shared memory (launched with 4096 bytes of it)
+    DeviceContext dctx;
+    CHECK(16, dctx.capacity() == 4096 && dctx.used() == 0);
+    auto tile = alloc<TSM, float>(dctx, Vector{2, 3}, Vector{3, 1});
+    CHECK(17, tile.valid() && tile.rank() == 2 && tile.get_shape(0) == 2 && tile.get_shape(1) == 3);
+    CHECK(18, tile.get_stride(0) == 3 && tile.get_stride(1) == 1 && tile.space() == MemorySpace::TSM);
+    bool zero = true;
+    for (int i = 0; i < 6; ++i) zero = zero && tile.data()[i] == 0.0f;
+    CHECK(19, zero);  // value-initialised, as the reference's alloc
+    barrier();
+    if (thread_id() == 0) tile.data()[0] = 7.0f;
+    barrier();
+    CHECK(20, tile.data()[0] == 7.0f);
+    const long long m = 4, n = 5;
+    auto dyn = alloc<GM, float>(dctx, Vector(m, n), Vector(n, 1));
+    CHECK(21, dyn.valid() && dyn.rank() == 2 && dyn.get_shape(0) == m && dyn.get_shape(1) == n && dyn.get_stride(0) == n &&
+              dyn.get_stride(1) == 1 && dyn.space() == MemorySpace::GM);
+    CHECK(22, (reinterpret_cast<uintptr_t>(dyn.data()) & 127u) == 0 && dyn.data() != tile.data());
+    const long long mark = dctx.mark();
+    CHECK(23, !alloc<TSM, float>(dctx, Vector(2000LL), Vector(1LL)).valid() && dctx.mark() == mark);  // 8000 bytes do not fit
+    auto again = alloc<TSM, float>(dctx, Vector(8LL), Vector(1LL));
+    dctx.release(mark);
+    CHECK(24, again.valid() && alloc<TSM, float>(dctx, Vector(8LL), Vector(1LL)).data() == again.data());  // released, reused
+    CHECK(25, !alloc<TSM, float>(dctx, Vector(2, 3), Vector(0, 1)).valid() && !alloc<TSM, float>(dctx, Vector(2, 3), Vector(3LL)).valid());
+    // a caller-owned arena
+    DeviceContext own(small_data, 40);
+    CHECK(26, alloc<TSM, int>(own, Vector(10LL), Vector(1LL)).data() == reinterpret_cast<int*>(small_data));
+    CHECK(27, !alloc<TSM, int>(own, Vector(1LL), Vector(1LL)).valid());  // the next 128-byte boundary is past the end
+}
+
+// The matmul loop nest in the multi-buffer form the reference's multi-buffer pass produces
+// (kernel_gen/passes/memory/multi_buffer.py): the lhs and rhs tiles of successive k steps rotate
+// through two-slot rings (make_ring / current / advance) carved with alloc, everything else as in
+// matmul_nest_kernel. The result must not depend on which slot a k step used.
+__global__ void matmul_ring_nest_kernel(float* out_p, const float* lhs_p, const float* rhs_p, const float* bias_p, long long H, long long K,
+                                        long long W, long long th, long long tw, long long tk, int* status) {
+    DevCtx ctx;
+    DeviceContext dctx;
+    Memory<GM, float> out(out_p, {H, W});
+    Memory<GM, float> lhs(const_cast<float*>(lhs_p), {H, K});
+    Memory<GM, float> rhs(const_cast<float*>(rhs_p), {K, W});
+    const long long lhs_stage = (th * tk * 4 + 127) / 128 * 128, rhs_stage = (tk * tw * 4 + 127) / 128 * 128;
+    int rc = 0;
+    for (long long h0 = block_id() * th; h0 < H; h0 += block_num() * th) {
+        for (long long w0 = 0; w0 < W; w0 += tw) {
+            const long long mark = dctx.mark();
+            const long long cur_h = min(th, H - h0), cur_w = min(tw, W - w0);
+            Memory<TSM, float> acc = alloc<TSM, float>(dctx, Vector(cur_h, cur_w), Vector(cur_w, 1));
+            Memory<TSM, float> partial = alloc<TSM, float>(dctx, Vector(cur_h, cur_w), Vector(cur_w, 1));
+            Memory<TSM, int8_t> lhs_backing = alloc<TSM, int8_t>(dctx, Vector(2 * lhs_stage), Vector(1LL));
+            Memory<TSM, int8_t> rhs_backing = alloc<TSM, int8_t>(dctx, Vector(2 * rhs_stage), Vector(1LL));
+            auto lhs_ring = make_ring<float>(lhs_backing, 2, lhs_stage, {th, tk}, {tk, 1});
+            auto rhs_ring = make_ring<float>(rhs_backing, 2, rhs_stage, {tk, tw}, {tw, 1});
+            if (!acc.valid() || !partial.valid() || !lhs_ring.valid() || !rhs_ring.valid()) rc |= 1;
+            Memory<TSM, float> lhs_slot = lhs_ring.current(), rhs_slot = rhs_ring.current();
+            for (long long k0 = 0; k0 < K; k0 += tk) {
+                const long long cur_k = min(tk, K - k0);
+                Memory<TSM, float> lhs_tile = lhs_slot.view<float>(Vector(0, 0), Vector(cur_h, cur_k), Vector(1, 1));
+                Memory<TSM, float> rhs_tile = rhs_slot.view<float>(Vector(0, 0), Vector(cur_k, cur_w), Vector(1, 1));
+                rc |= slice(ctx, lhs_tile, lhs, Vector(h0, k0), Vector(cur_h, cur_k), Vector(1, 1));
+                rc |= slice(ctx, rhs_tile, rhs, Vector(k0, w0), Vector(cur_k, cur_w), Vector(1, 1));
+                rc |= matmul<TSM, TSM, TSM, float, float, float>(ctx, partial, lhs_tile, rhs_tile);
+                rc |= add<TSM, float, float>(ctx, acc, acc, partial);
+                lhs_slot = lhs_ring.advance();
+                rhs_slot = rhs_ring.advance();
+            }
+            if (bias_p != nullptr) {
+                Memory<TSM, float> bias_tile = alloc<TSM, float>(dctx, Vector(cur_w), Vector(1LL));
+                Memory<TSM, float> bias_full = alloc<TSM, float>(dctx, Vector(cur_h, cur_w), Vector(cur_w, 1));
+                Memory<GM, float> bias(const_cast<float*>(bias_p), {W});
+                rc |= slice(ctx, bias_tile, bias, Vector(w0), Vector(cur_w), Vector(1LL));
+                Memory<TSM, float> bias_row = bias_tile.reshape({1, cur_w});
+                rc |= broadcast<TSM, TSM, float, float>(ctx, bias_full, bias_row);
+                rc |= add<TSM, float, float>(ctx, acc, acc, bias_full);
+            }
+            rc |= deslice(ctx, out, acc, Vector(h0, w0), Vector(cur_h, cur_w), Vector(1, 1));
+            dctx.release(mark);
+        }
+    }
+    if (rc != 0 && thread_id() == 0) atomicExch(status, 1);
+}
+
 // ---------------------------------------------------------------- conv2d loop nest
 // kernel/conv2d/inputs_dynamic_tile_dynamic.py:142-205, f-tiles block-strided.
 struct ConvArgs {
@@ -437,6 +561,22 @@ int kg_api_matmul(float* out, const float* lhs, const float* rhs, const float* b
     KernelContext ctx;
     ctx.synchronize = true;
     return launch<kGrid, kThreads, 1, kArenaBytes, matmul_nest_kernel>(ctx, out, lhs, rhs, bias, H, K, W, th, tw, tk, status);
+}
+
+int kg_api_ring_kat(int* codes) {
+    KernelContext ctx;
+    ctx.synchronize = true;
+    return launch<1, kThreads, 1, 4096, ring_alloc_kat_kernel>(ctx, codes);
+}
+
+int kg_api_matmul_ring(float* out, const float* lhs, const float* rhs, const float* bias, long long H, long long K, long long W, long long th,
+                       long long tw, long long tk, int* status) {
+    const auto up = [](long long b) { return (b + 127) / 128 * 128; };
+    const long long need = 3 * up(th * tw * 4) + 2 * up(th * tk * 4) + 2 * up(tk * tw * 4) + up(tw * 4) + 6 * 128;
+    if (need > kArenaBytes) return 2;
+    KernelContext ctx;
+    ctx.synchronize = true;
+    return launch<kGrid, kThreads, 1, kArenaBytes, matmul_ring_nest_kernel>(ctx, out, lhs, rhs, bias, H, K, W, th, tw, tk, status);
 }
 
 int kg_api_conv2d(float* out, const float* input, const float* weight, const float* bias, const long long* p, int* status) {

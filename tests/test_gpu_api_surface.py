@@ -30,7 +30,9 @@ def checks(cuda_device):
     lib.kg_api_matmul.argtypes = [vp, vp, vp, vp] + [ll] * 6 + [vp]
     lib.kg_api_conv2d.argtypes = [vp, vp, vp, vp, vp, vp]
     lib.kg_api_flash.argtypes = [vp, vp, vp, vp] + [ll] * 6 + [vp]
-    for f in (lib.kg_api_kat, lib.kg_api_matmul, lib.kg_api_conv2d, lib.kg_api_flash):
+    lib.kg_api_ring_kat.argtypes = [vp]
+    lib.kg_api_matmul_ring.argtypes = [vp, vp, vp, vp] + [ll] * 6 + [vp]
+    for f in (lib.kg_api_kat, lib.kg_api_matmul, lib.kg_api_conv2d, lib.kg_api_flash, lib.kg_api_ring_kat, lib.kg_api_matmul_ring):
         f.restype = ctypes.c_int
     return lib
 
@@ -54,6 +56,18 @@ def test_reference_known_answers_on_a_thread_block(checks, cuda_device):
     assert failed == [], f"failing known-answer checks: {failed}"
 
 
+def test_ring_and_alloc_known_answers_on_a_thread_block(checks, cuda_device):
+    """dma.make_ring / current / advance (slot order, byte offsets, the reference's rejections)
+    and dma.alloc (layout, zero fill, arena exhaustion and reuse), test_dma.py:225-297 and
+    :653-700 of the reference, on a thread block."""
+    import torch
+
+    codes = torch.zeros(64, dtype=torch.int32, device=cuda_device)
+    assert checks.kg_api_ring_kat(codes.data_ptr()) == 0
+    failed = torch.nonzero(codes).flatten().tolist()
+    assert failed == [], f"failing ring / alloc checks: {failed}"
+
+
 FP32_CASES = [c for c in golden_cases() if all(v.dtype == np.float32 for v in c[3].values())]
 
 
@@ -68,6 +82,23 @@ def test_matmul_loop_nest_on_helpers_bit_exact(checks, cuda_device, name, kind, 
     status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
     lhs, rhs, bias = (_dev(inputs.get(n), cuda_device) for n in ("lhs", "rhs", "bias"))  # kept alive across the call
     rc = checks.kg_api_matmul(out.data_ptr(), _ptr(lhs), _ptr(rhs), _ptr(bias), H, K, W, *params["tiles"], status.data_ptr())
+    assert rc == 0 and int(status.item()) == 0
+    np.testing.assert_array_equal(out.cpu().numpy(), gold)
+
+
+@pytest.mark.parametrize("name,kind,params,inputs", [c for c in FP32_CASES if c[1] == "matmul"], ids=lambda x: x if isinstance(x, str) else "")
+def test_double_buffered_matmul_nest_on_rings_bit_exact(checks, cuda_device, name, kind, params, inputs):
+    """The matmul nest with its lhs / rhs tiles rotating through two-slot rings carved by alloc
+    (the multi-buffer pass's form) equals the reference helpers' output bit for bit."""
+    import torch
+
+    gold = load_golden(name)["expected"]
+    H, K = inputs["lhs"].shape
+    W = inputs["rhs"].shape[1]
+    out = torch.full((H, W), float("nan"), device=cuda_device)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    lhs, rhs, bias = (_dev(inputs.get(n), cuda_device) for n in ("lhs", "rhs", "bias"))
+    rc = checks.kg_api_matmul_ring(out.data_ptr(), _ptr(lhs), _ptr(rhs), _ptr(bias), H, K, W, *params["tiles"], status.data_ptr())
     assert rc == 0 and int(status.item()) == 0
     np.testing.assert_array_equal(out.cpu().numpy(), gold)
 
