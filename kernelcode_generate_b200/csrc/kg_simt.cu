@@ -11,10 +11,15 @@
 //   flash_attn_simt     kernel/flash_attention/inputs_dynamic_tile_dynamic.py:117-195, online softmax
 #include "kg_simt.h"
 
+#include "kg_device_once.h"
+
+#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 
 namespace kg {
 namespace {
+
+namespace cg = cooperative_groups;
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
@@ -231,13 +236,23 @@ __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ ou
 }
 
 // ------------------------------------------------------------------ flash attention
-// One CTA = 16*RA query rows of one (b, h); 256 threads as 16 x 16 (ty, tx). Key/value tiles of 64
-// rows. Thread (ty, tx) owns scores rows RA*ty..RA*ty+RA-1 x keys 4tx..4tx+3 and the same output
-// rows x head columns tx, tx+16, ... (DT of them, D padded to 16*DT). Q and K are staged transposed
-// ([d][row]) so each step of Q.K^T is one RA-wide and one float4 shared load for 4*RA FMAs; P goes
-// through shared memory to the P.V product. Row max / sum combine over the 16 tx threads of a row
-// with shuffles. RA (4, 2 or 1 rows per thread) is chosen per call so small problems still spread
-// over the SMs: every output element is computed the same way whatever RA is.
+// One CTA = 16*RA query rows of one (b, h) and one range of keys; 256 threads as 16 x 16 (ty, tx).
+// Key/value tiles of 64 rows. Thread (ty, tx) owns scores rows RA*ty..RA*ty+RA-1 x keys
+// 4tx..4tx+3 and the same output rows x head columns tx, tx+16, ... (DT of them, D padded to
+// 16*DT). Q and K are staged transposed ([d][row]) so each step of Q.K^T is one RA-wide and one
+// float4 shared load for 4*RA FMAs; P goes through shared memory to the P.V product. Row max /
+// sum combine over the 16 tx threads of a row with shuffles. RA (4, 2 or 1 rows per thread) is
+// chosen per call so small problems still spread over the SMs.
+//
+// Key split: the grid's x dimension is (query tiles) x NS and the kernel runs in thread-block
+// clusters of NS CTAs along x (NS = 1 when there is no split). CTA rank r of a cluster walks keys
+// [r*key_split, (r+1)*key_split) of its query tile and keeps its partial state in shared memory:
+// the unnormalised O, the running max m (log2 domain) and the running sum l of every row. After a
+// cluster barrier each CTA merges BR/NS of the tile's rows across the NS partials, read from the
+// other CTAs' shared memory (distributed shared memory), with the online-softmax rescaling of
+// kernel/flash_attention/inputs_dynamic_tile_dynamic.py:143-195: M = max_r m_r,
+// L = sum_r l_r 2^(m_r - M), O = sum_r O_r 2^(m_r - M), out = O / L. The split lets a small
+// problem keep every SM busy with one or two dependent key steps per CTA instead of S/64.
 constexpr int FA_BC = 64;
 
 template <int RA>
@@ -253,27 +268,82 @@ __device__ __forceinline__ void load_rows(const float* p, float (&r)[RA]) {
     }
 }
 
-template <typename T, int DT, int RA>
+template <int DT, int RA>
+struct FaSmem {
+    static constexpr int DP = 16 * DT;
+    static constexpr int BR = 16 * RA;
+    static constexpr int LDQ = BR + 4;      // row pitch of the transposed Q tile
+    static constexpr int LDK = FA_BC + 4;   // row pitch of the transposed K tile
+    static constexpr int LDV = DP + 4;
+    static constexpr int LDP = BR + 4;      // row pitch of the transposed P tile ([key][row])
+    static constexpr size_t floats = (size_t)DP * LDQ + (size_t)DP * LDK + (size_t)FA_BC * LDV + (size_t)FA_BC * LDP + 2 * BR;
+    // Output columns a thread owns: with DT % 4 == 0, DT / 4 groups of 4 contiguous columns
+    // (64 g + 4 tx .. + 3), so each P.V step reads them as float4s; otherwise tx + 16 c.
+    static constexpr bool VEC_COLS = DT % 4 == 0;
+    __device__ static int col(int tx, int c) { return VEC_COLS ? 64 * (c >> 2) + 4 * tx + (c & 3) : tx + 16 * c; }
+    static_assert(BR * DP <= FA_BC * LDV, "the partial O of a split reuses the V tile");
+};
+
+// Vector tile loads (VEC: fp32 planes, D % 4 == 0, 16-byte aligned): float4 loads with index maps
+// that are shifts of the thread id. K and Q, which are stored transposed, put consecutive lanes on
+// consecutive rows so the scalar transposed stores hit distinct banks; V, stored as is, puts them
+// along a row (coalesced loads, conflict-free float4 stores). Out-of-range rows and columns of the
+// padded tile read as zero.
+__device__ __forceinline__ float4 ld4_or_zero(const float* p, bool ok) {
+    return ok ? __ldg(reinterpret_cast<const float4*>(p)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+}
+
+template <typename T, int DT, int RA, bool VEC>
 __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__ out, const T* __restrict__ q, const T* __restrict__ k,
-                                                              const T* __restrict__ v, int H, int S, int D, float scale_log2, int causal) {
-    constexpr int DP = 16 * DT;          // padded head dim
-    constexpr int BR = 16 * RA;          // query rows per CTA
-    constexpr int LDQ = BR + 4;          // row pitch of the transposed Q tile
-    constexpr int LDK = FA_BC + 4;       // row pitch of the transposed K tile
+                                                              const T* __restrict__ v, int H, int S, int D, float scale_log2, int causal,
+                                                              int key_split) {
+    using L = FaSmem<DT, RA>;
+    constexpr int DP = L::DP, BR = L::BR, LDQ = L::LDQ, LDK = L::LDK, LDV = L::LDV, LDP = L::LDP;
     extern __shared__ float4 fa_smem4[];
     float* fa_smem = reinterpret_cast<float*>(fa_smem4);
     float* sQt = fa_smem;                // [DP][LDQ]
     float* sKt = sQt + DP * LDQ;         // [DP][LDK]
-    float* sV = sKt + DP * LDK;          // [FA_BC][DP + 4]
-    float* sP = sV + FA_BC * (DP + 4);   // [BR][FA_BC + 4]
+    float* sV = sKt + DP * LDK;          // [FA_BC][LDV]; after the key loop, a split's partial O [BR][DP]
+    float* sP = sV + FA_BC * LDV;        // [FA_BC][LDP]: P transposed, a thread's RA rows contiguous
+    float* sM = sP + FA_BC * LDP;        // [BR]: a split's running max per row
+    float* sL = sM + BR;                 // [BR]: a split's running sum per row
+    cg::cluster_group cluster = cg::this_cluster();
+    const int ns = static_cast<int>(cluster.num_blocks());
+    const int split = static_cast<int>(cluster.block_rank());
     const int bh = blockIdx.y;
-    const int m0 = blockIdx.x * BR;
+    const int m0 = (blockIdx.x / ns) * BR;
     const size_t base = (size_t)bh * S * D;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
 
-    for (int i = threadIdx.x; i < BR * DP; i += 256) {
-        const int r = i / DP, d = i - r * DP;
-        sQt[d * LDQ + r] = (m0 + r < S && d < D) ? to_f32(q[base + (size_t)(m0 + r) * D + d]) : 0.0f;
+    // Q tile. Small tiles (at most 8 elements per thread): loads issued first and stored together
+    // with the first K/V tile, so the two share one round trip to memory. Larger ones are staged
+    // at once (holding them in registers across the K/V loads would spill).
+    constexpr int Q_PER = BR * DP / 256;
+    constexpr bool Q_PREFETCH = !VEC && Q_PER <= 8;
+    float qv[Q_PREFETCH ? Q_PER : 1];
+    constexpr int ROW4 = DP / 4;                          // float4 per padded row
+    constexpr int Q4 = (BR * ROW4 + 255) / 256;           // float4 of Q per thread (vector path)
+    float4 q4v[VEC ? Q4 : 1];
+    if constexpr (VEC) {
+        const float* qf = reinterpret_cast<const float*>(q) + base;
+#pragma unroll
+        for (int e = 0; e < Q4; ++e) {
+            const int i = threadIdx.x + 256 * e;
+            const int r = i % BR, c4 = i / BR;
+            q4v[e] = ld4_or_zero(qf + (size_t)(m0 + r) * D + 4 * c4, i < BR * ROW4 && m0 + r < S && 4 * c4 < D);
+        }
+    } else if constexpr (Q_PREFETCH) {
+#pragma unroll
+        for (int e = 0; e < Q_PER; ++e) {
+            const int i = threadIdx.x + 256 * e;
+            const int r = i / DP, d = i - r * DP;
+            qv[e] = (m0 + r < S && d < D) ? to_f32(q[base + (size_t)(m0 + r) * D + d]) : 0.0f;
+        }
+    } else {
+        for (int i = threadIdx.x; i < BR * DP; i += 256) {
+            const int r = i / DP, d = i - r * DP;
+            sQt[d * LDQ + r] = (m0 + r < S && d < D) ? to_f32(q[base + (size_t)(m0 + r) * D + d]) : 0.0f;
+        }
     }
     float o[RA][DT];
     float m_run[RA], l_run[RA];
@@ -284,16 +354,62 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
 #pragma unroll
         for (int c = 0; c < DT; ++c) o[a][c] = 0.0f;
     }
-    const int n_end = causal ? min(S, m0 + BR) : S;
-    for (int n0 = 0; n0 < n_end; n0 += FA_BC) {
+    const int k_begin = split * key_split;
+    const int k_end = min(causal ? min(S, m0 + BR) : S, k_begin + key_split);
+    bool q_stored = false;
+    for (int n0 = k_begin; n0 < k_end; n0 += FA_BC) {
         __syncthreads();
         // K and V tile: KV_PER elements of each per thread, loaded in chunks whose loads are all
         // issued before their shared-memory stores, so their latencies overlap.
+        if constexpr (VEC) {
+            constexpr int KV4 = FA_BC * ROW4 / 256;          // = DT float4 of K and of V per thread
+            constexpr int CH = KV4 <= 4 ? KV4 : (KV4 % 4 == 0 ? 4 : (KV4 % 3 == 0 ? 3 : (KV4 % 2 == 0 ? 2 : 1)));  // <= 4 float4 pairs in flight
+            static_assert(KV4 % CH == 0, "whole chunks");
+            const float* kf = reinterpret_cast<const float*>(k) + base;
+            const float* vf = reinterpret_cast<const float*>(v) + base;
+#pragma unroll
+            for (int e0 = 0; e0 < KV4; e0 += CH) {
+                float4 kr[CH], vr[CH];
+#pragma unroll
+                for (int e = 0; e < CH; ++e) {
+                    const int i = threadIdx.x + 256 * (e0 + e);
+                    const int kj = i % FA_BC, kc = i / FA_BC;  // K: lanes along keys
+                    const int vj = i / ROW4, vc = i % ROW4;    // V: lanes along the row
+                    kr[e] = ld4_or_zero(kf + (size_t)(n0 + kj) * D + 4 * kc, n0 + kj < S && 4 * kc < D);
+                    vr[e] = ld4_or_zero(vf + (size_t)(n0 + vj) * D + 4 * vc, n0 + vj < S && 4 * vc < D);
+                }
+                if (!q_stored) {
+#pragma unroll
+                    for (int e = 0; e < Q4; ++e) {
+                        const int i = threadIdx.x + 256 * e;
+                        const int r = i % BR, c4 = i / BR;
+                        if (i < BR * ROW4) {
+                            sQt[(4 * c4 + 0) * LDQ + r] = q4v[e].x;
+                            sQt[(4 * c4 + 1) * LDQ + r] = q4v[e].y;
+                            sQt[(4 * c4 + 2) * LDQ + r] = q4v[e].z;
+                            sQt[(4 * c4 + 3) * LDQ + r] = q4v[e].w;
+                        }
+                    }
+                    q_stored = true;
+                }
+#pragma unroll
+                for (int e = 0; e < CH; ++e) {
+                    const int i = threadIdx.x + 256 * (e0 + e);
+                    const int kj = i % FA_BC, kc = i / FA_BC;
+                    const int vj = i / ROW4, vc = i % ROW4;
+                    sKt[(4 * kc + 0) * LDK + kj] = kr[e].x;
+                    sKt[(4 * kc + 1) * LDK + kj] = kr[e].y;
+                    sKt[(4 * kc + 2) * LDK + kj] = kr[e].z;
+                    sKt[(4 * kc + 3) * LDK + kj] = kr[e].w;
+                    *reinterpret_cast<float4*>(sV + vj * LDV + 4 * vc) = vr[e];
+                }
+            }
+        }
         constexpr int KV_PER = FA_BC * DP / 256;
         constexpr int KV_CH = KV_PER <= 16 ? KV_PER : KV_PER / 2;  // KV_PER = 4 * DT <= 32
         static_assert(KV_PER % KV_CH == 0, "whole chunks");
 #pragma unroll
-        for (int e0 = 0; e0 < KV_PER; e0 += KV_CH) {
+        for (int e0 = 0; e0 < (VEC ? 0 : KV_PER); e0 += KV_CH) {
             float kv[KV_CH], vv[KV_CH];
 #pragma unroll
             for (int e = 0; e < KV_CH; ++e) {
@@ -303,28 +419,41 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
                 kv[e] = ok ? to_f32(k[base + (size_t)(n0 + j) * D + d]) : 0.0f;
                 vv[e] = ok ? to_f32(v[base + (size_t)(n0 + j) * D + d]) : 0.0f;
             }
+            if constexpr (Q_PREFETCH) {
+                if (!q_stored) {
+#pragma unroll
+                    for (int e = 0; e < Q_PER; ++e) {
+                        const int i = threadIdx.x + 256 * e;
+                        const int r = i / DP, d = i - r * DP;
+                        sQt[d * LDQ + r] = qv[e];
+                    }
+                    q_stored = true;
+                }
+            }
 #pragma unroll
             for (int e = 0; e < KV_CH; ++e) {
                 const int i = threadIdx.x + 256 * (e0 + e);
                 const int j = i / DP, d = i - j * DP;
                 sKt[d * LDK + j] = kv[e];
-                sV[j * (DP + 4) + d] = vv[e];
+                sV[j * LDV + d] = vv[e];
             }
         }
         __syncthreads();
         float sc[RA][4] = {};
 #pragma unroll 4
         for (int d = 0; d < DP; ++d) {
-            float qv[RA];
-            load_rows<RA>(sQt + d * LDQ + RA * ty, qv);
+            float qr[RA];
+            load_rows<RA>(sQt + d * LDQ + RA * ty, qr);
             const float4 kb = *reinterpret_cast<const float4*>(sKt + d * LDK + 4 * tx);
-            const float kv[4] = {kb.x, kb.y, kb.z, kb.w};
+            const float kk[4] = {kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
             for (int a = 0; a < RA; ++a)
 #pragma unroll
-                for (int b = 0; b < 4; ++b) sc[a][b] = fmaf(qv[a], kv[b], sc[a][b]);
+                for (int b = 0; b < 4; ++b) sc[a][b] = fmaf(qr[a], kk[b], sc[a][b]);
         }
         float alpha[RA];
+        // Tiles wholly inside the key range and (causal) wholly at or below the diagonal need no mask.
+        const bool masked = n0 + FA_BC > k_end || (causal && n0 + FA_BC - 1 > m0);
 #pragma unroll
         for (int a = 0; a < RA; ++a) {
             const int row = m0 + RA * ty + a;
@@ -332,7 +461,7 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
                 const int key = n0 + 4 * tx + b;
-                const bool valid = key < S && !(causal && key > row);
+                const bool valid = !masked || (key < k_end && !(causal && key > row));
                 sc[a][b] = valid ? sc[a][b] * scale_log2 : -INFINITY;
                 mx = fmaxf(mx, sc[a][b]);
             }
@@ -345,14 +474,26 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
             float psum = 0.0f;
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
-                const float p = exp2f(sc[a][b] - m_use);
-                psum += p;
-                sP[(RA * ty + a) * (FA_BC + 4) + 4 * tx + b] = p;
+                const float pb = exp2f(sc[a][b] - m_use);
+                psum += pb;
+                sc[a][b] = pb;
             }
 #pragma unroll
             for (int off = 1; off < 16; off <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
             l_run[a] = l_run[a] * alpha[a] + psum;
             m_run[a] = m_new;
+        }
+        // P transposed: key 4tx+b, this thread's RA consecutive rows as one vector store.
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            float* dst = sP + (4 * tx + b) * LDP + RA * ty;
+            if constexpr (RA == 4) {
+                *reinterpret_cast<float4*>(dst) = make_float4(sc[0][b], sc[1][b], sc[2][b], sc[3][b]);
+            } else if constexpr (RA == 2) {
+                *reinterpret_cast<float2*>(dst) = make_float2(sc[0][b], sc[1][b]);
+            } else {
+                dst[0] = sc[0][b];
+            }
         }
         __syncthreads();
 #pragma unroll
@@ -362,27 +503,72 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
 #pragma unroll 4
         for (int j = 0; j < FA_BC; ++j) {
             float pv[RA];
+            load_rows<RA>(sP + j * LDP + RA * ty, pv);
+            if constexpr (L::VEC_COLS) {
 #pragma unroll
-            for (int a = 0; a < RA; ++a) pv[a] = sP[(RA * ty + a) * (FA_BC + 4) + j];
+                for (int g = 0; g < DT / 4; ++g) {
+                    const float4 v4 = *reinterpret_cast<const float4*>(sV + j * LDV + 64 * g + 4 * tx);
+                    const float vj[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
-            for (int c = 0; c < DT; ++c) {
-                const float vv = sV[j * (DP + 4) + tx + 16 * c];
+                    for (int e = 0; e < 4; ++e)
 #pragma unroll
-                for (int a = 0; a < RA; ++a) o[a][c] = fmaf(pv[a], vv, o[a][c]);
+                        for (int a = 0; a < RA; ++a) o[a][4 * g + e] = fmaf(pv[a], vj[e], o[a][4 * g + e]);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < DT; ++c) {
+                    const float vj = sV[j * LDV + tx + 16 * c];
+#pragma unroll
+                    for (int a = 0; a < RA; ++a) o[a][c] = fmaf(pv[a], vj, o[a][c]);
+                }
             }
         }
     }
+    if (ns == 1) {
+#pragma unroll
+        for (int a = 0; a < RA; ++a) {
+            const int row = m0 + RA * ty + a;
+            if (row >= S) continue;
+            const float inv = 1.0f / l_run[a];
+#pragma unroll
+            for (int c = 0; c < DT; ++c) {
+                const int d = L::col(tx, c);
+                if (d < D) store_out(out + base + (size_t)row * D + d, o[a][c] * inv);
+            }
+        }
+        return;
+    }
+    // Key split: publish this CTA's partial state, then merge rows across the cluster.
+    __syncthreads();  // the last key tile's V is no longer read
+    float* sO = sV;   // [BR][DP]
 #pragma unroll
     for (int a = 0; a < RA; ++a) {
-        const int row = m0 + RA * ty + a;
-        if (row >= S) continue;
-        const float inv = 1.0f / l_run[a];
+        const int r = RA * ty + a;
 #pragma unroll
-        for (int c = 0; c < DT; ++c) {
-            const int d = tx + 16 * c;
-            if (d < D) store_out(out + base + (size_t)row * D + d, o[a][c] * inv);
+        for (int c = 0; c < DT; ++c) sO[r * DP + L::col(tx, c)] = o[a][c];
+        if (tx == 0) {
+            sM[r] = m_run[a];
+            sL[r] = l_run[a];
         }
     }
+    cluster.sync();
+    const int rows_per = BR / ns;
+    for (int e = threadIdx.x; e < rows_per * DP; e += 256) {
+        const int r = split * rows_per + e / DP, d = e % DP;
+        const int row = m0 + r;
+        if (row >= S || d >= D) continue;
+        float mmax = -INFINITY;
+        for (int t = 0; t < ns; ++t) mmax = fmaxf(mmax, *cluster.map_shared_rank(sM + r, t));
+        float lsum = 0.0f, osum = 0.0f;
+        for (int t = 0; t < ns; ++t) {
+            const float mt = *cluster.map_shared_rank(sM + r, t);
+            const float w = mt == -INFINITY ? 0.0f : exp2f(mt - mmax);
+            lsum = fmaf(*cluster.map_shared_rank(sL + r, t), w, lsum);
+            osum = fmaf(*cluster.map_shared_rank(sO + r * DP + d, t), w, osum);
+        }
+        store_out(out + base + (size_t)row * D + d, osum / lsum);
+    }
+    cluster.sync();  // no CTA leaves while the others still read its shared memory
 }
 
 }  // namespace
@@ -435,55 +621,94 @@ template cudaError_t conv2d_simt_launch<__nv_bfloat16>(float*, const __nv_bfloat
 
 template <typename T, int DT, int RA>
 static cudaError_t flash_attn_simt_launch_ra(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
-                                             cudaStream_t stream) {
-    constexpr int DP = 16 * DT, BR = 16 * RA;
-    const size_t smem = sizeof(float) * ((size_t)DP * (BR + 4) + (size_t)DP * (FA_BC + 4) + (size_t)FA_BC * (DP + 4) + (size_t)BR * (FA_BC + 4));
-    cudaError_t e = cudaFuncSetAttribute(flash_attn_simt_kernel<T, DT, RA>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                                             int ns, cudaStream_t stream) {
+    using L = FaSmem<DT, RA>;
+    const size_t smem = sizeof(float) * L::floats;
+    // fp32 planes with D % 4 == 0 and 16-byte aligned bases take the float4 tile loads.
+    constexpr bool kF32 = sizeof(T) == 4;
+    const bool vec = kF32 && D % 4 == 0 && ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                                             reinterpret_cast<uintptr_t>(v)) & 15u) == 0;
+    auto kernel = vec ? flash_attn_simt_kernel<T, DT, RA, kF32> : flash_attn_simt_kernel<T, DT, RA, false>;
+    static DeviceOnce attr_once[2];
+    cudaError_t e = attr_once[vec ? 1 : 0].run([smem, kernel] {
+        return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    });
     if (e != cudaSuccess) return e;
-    dim3 grid((S + BR - 1) / BR, B * H);
+    const int q_tiles = (S + L::BR - 1) / L::BR;
+    const int key_split = ((S + ns - 1) / ns + FA_BC - 1) / FA_BC * FA_BC;
     const float scale_log2 = scale * 1.4426950408889634f;  // scores in the exp2 domain
-    flash_attn_simt_kernel<T, DT, RA><<<grid, 256, smem, stream>>>(out, q, k, v, H, S, D, scale_log2, causal);
-    return cudaGetLastError();
-}
-
-// Rows per thread: 4 (64-row query tiles) when that gives at least one CTA per SM; else 2 when
-// 32-row tiles fill half the SMs; else 1. C3 (1 x 8 x 512 x 64): 64, 128 or 256 CTAs took 75.8,
-// 57.3 and 65.6 us; 1 x 4 x 300 x 40: 43.0, 30.7 and 29.7 us.
-static int flash_attn_simt_rows_per_thread(int B, int H, int S) {
-    const long long bh = static_cast<long long>(B) * H;
-    if ((S + 63) / 64 * bh >= 148) return 4;
-    if ((S + 31) / 32 * bh >= 74) return 2;
-    return 1;
+    dim3 grid(static_cast<unsigned>(q_tiles * ns), static_cast<unsigned>(B * H));
+    if (ns == 1) {
+        kernel<<<grid, 256, smem, stream>>>(out, q, k, v, H, S, D, scale_log2, causal, key_split);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(ns);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, out, q, k, v, H, S, D, scale_log2, causal, key_split);
 }
 
 template <typename T, int DT>
 static cudaError_t flash_attn_simt_launch_dt(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
-                                             cudaStream_t stream) {
-    switch (flash_attn_simt_rows_per_thread(B, H, S)) {
-        case 4: return flash_attn_simt_launch_ra<T, DT, 4>(out, q, k, v, B, H, S, D, scale, causal, stream);
-        case 2: return flash_attn_simt_launch_ra<T, DT, 2>(out, q, k, v, B, H, S, D, scale, causal, stream);
-        default: return flash_attn_simt_launch_ra<T, DT, 1>(out, q, k, v, B, H, S, D, scale, causal, stream);
+                                             int ra, int ns, cudaStream_t stream) {
+    switch (ra) {
+        case 4: return flash_attn_simt_launch_ra<T, DT, 4>(out, q, k, v, B, H, S, D, scale, causal, ns, stream);
+        case 2: return flash_attn_simt_launch_ra<T, DT, 2>(out, q, k, v, B, H, S, D, scale, causal, ns, stream);
+        case 1: return flash_attn_simt_launch_ra<T, DT, 1>(out, q, k, v, B, H, S, D, scale, causal, ns, stream);
+        default: return cudaErrorInvalidValue;
     }
+}
+
+template <typename T>
+cudaError_t flash_attn_simt_launch_cfg(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
+                                       int ra, int ns, cudaStream_t stream) {
+    if (!(ns == 1 || ns == 2 || ns == 4 || ns == 8)) return cudaErrorInvalidValue;
+    switch ((D + 15) / 16) {
+        case 1: return flash_attn_simt_launch_dt<T, 1>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
+        case 2: return flash_attn_simt_launch_dt<T, 2>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
+        case 3: return flash_attn_simt_launch_dt<T, 3>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
+        case 4: return flash_attn_simt_launch_dt<T, 4>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
+        case 5: return flash_attn_simt_launch_dt<T, 5>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
+        case 6: return flash_attn_simt_launch_dt<T, 6>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
+        case 7: return flash_attn_simt_launch_dt<T, 7>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
+        case 8: return flash_attn_simt_launch_dt<T, 8>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+FlashSimtConfig flash_attn_simt_config(int B, int H, int S) {
+    // Rows per thread: 4 (64-row query tiles) when that gives at least one CTA per SM; else 2 when
+    // 32-row tiles fill half the SMs; else 1. Then, while fewer than 148 CTAs would run and each
+    // would walk more than one 64-key tile, the keys are split over 2, 4 or 8 CTAs of a cluster.
+    const long long bh = static_cast<long long>(B) * H;
+    FlashSimtConfig c{1, 1};
+    if ((S + 63) / 64 * bh >= 148) c.ra = 4;
+    else if ((S + 31) / 32 * bh >= 74) c.ra = 2;
+    const long long tiles = (S + 16 * c.ra - 1) / (16 * c.ra) * bh;
+    while (c.ns < 8 && tiles * c.ns < 148 && (S + c.ns - 1) / c.ns > FA_BC) c.ns *= 2;
+    return c;
 }
 
 template <typename T>
 cudaError_t flash_attn_simt_launch(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
                                    cudaStream_t stream) {
-    switch ((D + 15) / 16) {
-        case 1: return flash_attn_simt_launch_dt<T, 1>(out, q, k, v, B, H, S, D, scale, causal, stream);
-        case 2: return flash_attn_simt_launch_dt<T, 2>(out, q, k, v, B, H, S, D, scale, causal, stream);
-        case 3: return flash_attn_simt_launch_dt<T, 3>(out, q, k, v, B, H, S, D, scale, causal, stream);
-        case 4: return flash_attn_simt_launch_dt<T, 4>(out, q, k, v, B, H, S, D, scale, causal, stream);
-        case 5: return flash_attn_simt_launch_dt<T, 5>(out, q, k, v, B, H, S, D, scale, causal, stream);
-        case 6: return flash_attn_simt_launch_dt<T, 6>(out, q, k, v, B, H, S, D, scale, causal, stream);
-        case 7: return flash_attn_simt_launch_dt<T, 7>(out, q, k, v, B, H, S, D, scale, causal, stream);
-        case 8: return flash_attn_simt_launch_dt<T, 8>(out, q, k, v, B, H, S, D, scale, causal, stream);
-        default: return cudaErrorInvalidValue;
-    }
+    const FlashSimtConfig c = flash_attn_simt_config(B, H, S);
+    return flash_attn_simt_launch_cfg(out, q, k, v, B, H, S, D, scale, causal, c.ra, c.ns, stream);
 }
 template cudaError_t flash_attn_simt_launch<float>(float*, const float*, const float*, const float*, int, int, int, int, float, int,
                                                    cudaStream_t);
 template cudaError_t flash_attn_simt_launch<__nv_bfloat16>(__nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*,
                                                            const __nv_bfloat16*, int, int, int, int, float, int, cudaStream_t);
+template cudaError_t flash_attn_simt_launch_cfg<float>(float*, const float*, const float*, const float*, int, int, int, int, float, int, int,
+                                                       int, cudaStream_t);
 
 }  // namespace kg

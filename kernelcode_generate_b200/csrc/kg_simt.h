@@ -22,4 +22,15 @@ template <typename T>
 cudaError_t flash_attn_simt_launch(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
                                    cudaStream_t stream);
 
+// Launch shape of the CUDA-core attention kernel: `ra` query rows per thread (16 * ra per CTA) and
+// `ns` CTAs per thread-block cluster sharing each query tile's keys (1, 2, 4 or 8).
+struct FlashSimtConfig {
+    int ra;
+    int ns;
+};
+FlashSimtConfig flash_attn_simt_config(int B, int H, int S);
+template <typename T>
+cudaError_t flash_attn_simt_launch_cfg(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
+                                       int ra, int ns, cudaStream_t stream);
+
 }  // namespace kg
