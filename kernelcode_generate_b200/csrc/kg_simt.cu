@@ -236,13 +236,14 @@ __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ ou
 }
 
 // ------------------------------------------------------------------ flash attention
-// One CTA = 16*RA query rows of one (b, h) and one range of keys; 256 threads as 16 x 16 (ty, tx).
-// Key/value tiles of 64 rows. Thread (ty, tx) owns scores rows RA*ty..RA*ty+RA-1 x keys
-// 4tx..4tx+3 and the same output rows x head columns tx, tx+16, ... (DT of them, D padded to
-// 16*DT). Q and K are staged transposed ([d][row]) so each step of Q.K^T is one RA-wide and one
-// float4 shared load for 4*RA FMAs; P goes through shared memory to the P.V product. Row max /
-// sum combine over the 16 tx threads of a row with shuffles. RA (4, 2 or 1 rows per thread) is
-// chosen per call so small problems still spread over the SMs.
+// One CTA = 16*RA query rows of one (b, h) and one range of keys, walked in tiles of 64*KQ keys;
+// 256 threads as 16 x 16 (ty, tx). Thread (ty, tx) owns the scores of rows RA*ty..RA*ty+RA-1 x
+// keys 64q + 4tx .. 64q + 4tx + 3 (q < KQ), and the same rows x DT head columns of the output
+// (D padded to 16*DT). Q, K and P are staged transposed ([d][row], [d][key], [key][row]) so every
+// step of Q.K^T reads the thread's RA rows and 4*KQ keys, and every step of P.V its RA rows and
+// columns, as 16-byte shared loads: 4*RA*KQ FMAs per step for RA/4 + KQ loads. Row max / sum
+// combine over the 16 tx threads of a row with shuffles. Small problems use 8 rows x 8 keys per
+// thread (64 accumulators, one CTA per SM), larger ones 4 x 4.
 //
 // Key split: the grid's x dimension is (query tiles) x NS and the kernel runs in thread-block
 // clusters of NS CTAs along x (NS = 1 when there is no split). CTA rank r of a cluster walks keys
@@ -252,14 +253,17 @@ __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ ou
 // other CTAs' shared memory (distributed shared memory), with the online-softmax rescaling of
 // kernel/flash_attention/inputs_dynamic_tile_dynamic.py:143-195: M = max_r m_r,
 // L = sum_r l_r 2^(m_r - M), O = sum_r O_r 2^(m_r - M), out = O / L. The split lets a small
-// problem keep every SM busy with one or two dependent key steps per CTA instead of S/64.
-constexpr int FA_BC = 64;
+// problem keep every SM busy with one or two dependent key steps per CTA instead of S/BC.
 
+// RA consecutive floats from shared memory (16-byte loads when RA is a multiple of 4).
 template <int RA>
 __device__ __forceinline__ void load_rows(const float* p, float (&r)[RA]) {
-    if constexpr (RA == 4) {
-        const float4 t = *reinterpret_cast<const float4*>(p);
-        r[0] = t.x, r[1] = t.y, r[2] = t.z, r[3] = t.w;
+    if constexpr (RA % 4 == 0) {
+#pragma unroll
+        for (int g = 0; g < RA / 4; ++g) {
+            const float4 t = *reinterpret_cast<const float4*>(p + 4 * g);
+            r[4 * g] = t.x, r[4 * g + 1] = t.y, r[4 * g + 2] = t.z, r[4 * g + 3] = t.w;
+        }
     } else if constexpr (RA == 2) {
         const float2 t = *reinterpret_cast<const float2*>(p);
         r[0] = t.x, r[1] = t.y;
@@ -268,21 +272,51 @@ __device__ __forceinline__ void load_rows(const float* p, float (&r)[RA]) {
     }
 }
 
-template <int DT, int RA>
-struct FaSmem {
-    static constexpr int DP = 16 * DT;
-    static constexpr int BR = 16 * RA;
+template <int RA>
+__device__ __forceinline__ void store_rows(float* p, const float (&r)[RA]) {
+    if constexpr (RA % 4 == 0) {
+#pragma unroll
+        for (int g = 0; g < RA / 4; ++g)
+            *reinterpret_cast<float4*>(p + 4 * g) = make_float4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]);
+    } else if constexpr (RA == 2) {
+        *reinterpret_cast<float2*>(p) = make_float2(r[0], r[1]);
+    } else {
+        p[0] = r[0];
+    }
+}
+
+template <int DT, int RA, int KQ>
+struct FaCfg {
+    static constexpr int DP = 16 * DT;      // padded head dim
+    static constexpr int BR = 16 * RA;      // query rows per CTA
+    static constexpr int BC = 64 * KQ;      // keys per tile
     static constexpr int LDQ = BR + 4;      // row pitch of the transposed Q tile
-    static constexpr int LDK = FA_BC + 4;   // row pitch of the transposed K tile
+    static constexpr int LDK = BC + 4;      // row pitch of the transposed K tile
     static constexpr int LDV = DP + 4;
     static constexpr int LDP = BR + 4;      // row pitch of the transposed P tile ([key][row])
-    static constexpr size_t floats = (size_t)DP * LDQ + (size_t)DP * LDK + (size_t)FA_BC * LDV + (size_t)FA_BC * LDP + 2 * BR;
+    static constexpr size_t floats = (size_t)DP * LDQ + (size_t)DP * LDK + (size_t)BC * LDV + (size_t)BC * LDP + 2 * BR;
     // Output columns a thread owns: with DT % 4 == 0, DT / 4 groups of 4 contiguous columns
     // (64 g + 4 tx .. + 3), so each P.V step reads them as float4s; otherwise tx + 16 c.
     static constexpr bool VEC_COLS = DT % 4 == 0;
     __device__ static int col(int tx, int c) { return VEC_COLS ? 64 * (c >> 2) + 4 * tx + (c & 3) : tx + 16 * c; }
-    static_assert(BR * DP <= FA_BC * LDV, "the partial O of a split reuses the V tile");
+    static_assert(BR * DP <= BC * LDV, "the partial O of a split reuses the V tile");
+    static constexpr int MIN_BLOCKS = RA * KQ >= 16 ? 1 : 2;  // 64 accumulators: one CTA per SM, registers to spare
 };
+
+// The largest divisor of n that is at most cap (load chunks that split a tile evenly).
+constexpr int largest_divisor_upto(int n, int cap) {
+    for (int d = cap < n ? cap : n; d > 1; --d)
+        if (n % d == 0) return d;
+    return 1;
+}
+
+// 2^x with the hardware approximation (relative error about 2^-22; subnormal results flush to
+// zero, which the softmax weights never need).
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 // Vector tile loads (VEC: fp32 planes, D % 4 == 0, 16-byte aligned): float4 loads with index maps
 // that are shifts of the thread id. K and Q, which are stored transposed, put consecutive lanes on
@@ -293,19 +327,20 @@ __device__ __forceinline__ float4 ld4_or_zero(const float* p, bool ok) {
     return ok ? __ldg(reinterpret_cast<const float4*>(p)) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 }
 
-template <typename T, int DT, int RA, bool VEC>
-__global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__ out, const T* __restrict__ q, const T* __restrict__ k,
-                                                              const T* __restrict__ v, int H, int S, int D, float scale_log2, int causal,
-                                                              int key_split) {
-    using L = FaSmem<DT, RA>;
-    constexpr int DP = L::DP, BR = L::BR, LDQ = L::LDQ, LDK = L::LDK, LDV = L::LDV, LDP = L::LDP;
+template <typename T, int DT, int RA, int KQ, bool VEC>
+__global__ void __launch_bounds__(256, FaCfg<DT, RA, KQ>::MIN_BLOCKS)
+    flash_attn_simt_kernel(T* __restrict__ out, const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, int H, int S,
+                           int D, float scale_log2, int causal, int key_split) {
+    using L = FaCfg<DT, RA, KQ>;
+    constexpr int DP = L::DP, BR = L::BR, BC = L::BC, LDQ = L::LDQ, LDK = L::LDK, LDV = L::LDV, LDP = L::LDP;
+    constexpr int NK = 4 * KQ;           // keys per thread and tile
     extern __shared__ float4 fa_smem4[];
     float* fa_smem = reinterpret_cast<float*>(fa_smem4);
     float* sQt = fa_smem;                // [DP][LDQ]
     float* sKt = sQt + DP * LDQ;         // [DP][LDK]
-    float* sV = sKt + DP * LDK;          // [FA_BC][LDV]; after the key loop, a split's partial O [BR][DP]
-    float* sP = sV + FA_BC * LDV;        // [FA_BC][LDP]: P transposed, a thread's RA rows contiguous
-    float* sM = sP + FA_BC * LDP;        // [BR]: a split's running max per row
+    float* sV = sKt + DP * LDK;          // [BC][LDV]; after the key loop, a split's partial O [BR][DP]
+    float* sP = sV + BC * LDV;           // [BC][LDP]: P transposed, a thread's RA rows contiguous
+    float* sM = sP + BC * LDP;           // [BR]: a split's running max per row
     float* sL = sM + BR;                 // [BR]: a split's running sum per row
     cg::cluster_group cluster = cg::this_cluster();
     const int ns = static_cast<int>(cluster.num_blocks());
@@ -315,9 +350,9 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
     const size_t base = (size_t)bh * S * D;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
 
-    // Q tile. Small tiles (at most 8 elements per thread): loads issued first and stored together
-    // with the first K/V tile, so the two share one round trip to memory. Larger ones are staged
-    // at once (holding them in registers across the K/V loads would spill).
+    // Q tile. Vector path and small scalar tiles: loads issued first and stored together with the
+    // first K/V tile, so the two share one round trip to memory. Larger scalar tiles are staged at
+    // once (holding them in registers across the K/V loads would spill).
     constexpr int Q_PER = BR * DP / 256;
     constexpr bool Q_PREFETCH = !VEC && Q_PER <= 8;
     float qv[Q_PREFETCH ? Q_PER : 1];
@@ -356,14 +391,12 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
     }
     const int k_begin = split * key_split;
     const int k_end = min(causal ? min(S, m0 + BR) : S, k_begin + key_split);
-    bool q_stored = false;
-    for (int n0 = k_begin; n0 < k_end; n0 += FA_BC) {
+    bool q_stored = !(VEC || Q_PREFETCH);
+    for (int n0 = k_begin; n0 < k_end; n0 += BC) {
         __syncthreads();
-        // K and V tile: KV_PER elements of each per thread, loaded in chunks whose loads are all
-        // issued before their shared-memory stores, so their latencies overlap.
         if constexpr (VEC) {
-            constexpr int KV4 = FA_BC * ROW4 / 256;          // = DT float4 of K and of V per thread
-            constexpr int CH = KV4 <= 4 ? KV4 : (KV4 % 4 == 0 ? 4 : (KV4 % 3 == 0 ? 3 : (KV4 % 2 == 0 ? 2 : 1)));  // <= 4 float4 pairs in flight
+            constexpr int KV4 = BC * ROW4 / 256;             // = KQ * DT float4 of K and of V per thread
+            constexpr int CH = largest_divisor_upto(KV4, 4);  // at most 4 float4 pairs in flight
             static_assert(KV4 % CH == 0, "whole chunks");
             const float* kf = reinterpret_cast<const float*>(k) + base;
             const float* vf = reinterpret_cast<const float*>(v) + base;
@@ -373,7 +406,7 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
 #pragma unroll
                 for (int e = 0; e < CH; ++e) {
                     const int i = threadIdx.x + 256 * (e0 + e);
-                    const int kj = i % FA_BC, kc = i / FA_BC;  // K: lanes along keys
+                    const int kj = i % BC, kc = i / BC;        // K: lanes along keys
                     const int vj = i / ROW4, vc = i % ROW4;    // V: lanes along the row
                     kr[e] = ld4_or_zero(kf + (size_t)(n0 + kj) * D + 4 * kc, n0 + kj < S && 4 * kc < D);
                     vr[e] = ld4_or_zero(vf + (size_t)(n0 + vj) * D + 4 * vc, n0 + vj < S && 4 * vc < D);
@@ -395,7 +428,7 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
 #pragma unroll
                 for (int e = 0; e < CH; ++e) {
                     const int i = threadIdx.x + 256 * (e0 + e);
-                    const int kj = i % FA_BC, kc = i / FA_BC;
+                    const int kj = i % BC, kc = i / BC;
                     const int vj = i / ROW4, vc = i % ROW4;
                     sKt[(4 * kc + 0) * LDK + kj] = kr[e].x;
                     sKt[(4 * kc + 1) * LDK + kj] = kr[e].y;
@@ -404,104 +437,110 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
                     *reinterpret_cast<float4*>(sV + vj * LDV + 4 * vc) = vr[e];
                 }
             }
-        }
-        constexpr int KV_PER = FA_BC * DP / 256;
-        constexpr int KV_CH = KV_PER <= 16 ? KV_PER : KV_PER / 2;  // KV_PER = 4 * DT <= 32
-        static_assert(KV_PER % KV_CH == 0, "whole chunks");
+        } else {
+            // Scalar path: KV_PER elements of K and of V per thread, loaded in chunks whose loads
+            // are all issued before their shared-memory stores, so their latencies overlap.
+            constexpr int KV_PER = BC * DP / 256;
+            constexpr int KV_CH = largest_divisor_upto(KV_PER, 16);
+            static_assert(KV_PER % KV_CH == 0, "whole chunks");
 #pragma unroll
-        for (int e0 = 0; e0 < (VEC ? 0 : KV_PER); e0 += KV_CH) {
-            float kv[KV_CH], vv[KV_CH];
+            for (int e0 = 0; e0 < KV_PER; e0 += KV_CH) {
+                float kv[KV_CH], vv[KV_CH];
 #pragma unroll
-            for (int e = 0; e < KV_CH; ++e) {
-                const int i = threadIdx.x + 256 * (e0 + e);
-                const int j = i / DP, d = i - j * DP;
-                const bool ok = n0 + j < S && d < D;
-                kv[e] = ok ? to_f32(k[base + (size_t)(n0 + j) * D + d]) : 0.0f;
-                vv[e] = ok ? to_f32(v[base + (size_t)(n0 + j) * D + d]) : 0.0f;
-            }
-            if constexpr (Q_PREFETCH) {
-                if (!q_stored) {
-#pragma unroll
-                    for (int e = 0; e < Q_PER; ++e) {
-                        const int i = threadIdx.x + 256 * e;
-                        const int r = i / DP, d = i - r * DP;
-                        sQt[d * LDQ + r] = qv[e];
-                    }
-                    q_stored = true;
+                for (int e = 0; e < KV_CH; ++e) {
+                    const int i = threadIdx.x + 256 * (e0 + e);
+                    const int j = i / DP, d = i - j * DP;
+                    const bool ok = n0 + j < S && d < D;
+                    kv[e] = ok ? to_f32(k[base + (size_t)(n0 + j) * D + d]) : 0.0f;
+                    vv[e] = ok ? to_f32(v[base + (size_t)(n0 + j) * D + d]) : 0.0f;
                 }
-            }
+                if constexpr (Q_PREFETCH) {
+                    if (!q_stored) {
 #pragma unroll
-            for (int e = 0; e < KV_CH; ++e) {
-                const int i = threadIdx.x + 256 * (e0 + e);
-                const int j = i / DP, d = i - j * DP;
-                sKt[d * LDK + j] = kv[e];
-                sV[j * LDV + d] = vv[e];
+                        for (int e = 0; e < Q_PER; ++e) {
+                            const int i = threadIdx.x + 256 * e;
+                            const int r = i / DP, d = i - r * DP;
+                            sQt[d * LDQ + r] = qv[e];
+                        }
+                        q_stored = true;
+                    }
+                }
+#pragma unroll
+                for (int e = 0; e < KV_CH; ++e) {
+                    const int i = threadIdx.x + 256 * (e0 + e);
+                    const int j = i / DP, d = i - j * DP;
+                    sKt[d * LDK + j] = kv[e];
+                    sV[j * LDV + d] = vv[e];
+                }
             }
         }
         __syncthreads();
-        float sc[RA][4] = {};
-#pragma unroll 4
+        float sc[RA][NK] = {};
+        // Loop bodies of about 128 FMAs: fully unrolled loops of the larger register tiles overflow
+        // the instruction cache (ncu: `no_instruction` stalls).
+        constexpr int QK_UNROLL = 128 / (RA * NK) > 1 ? 128 / (RA * NK) : 1;
+        constexpr int PV_UNROLL = 128 / (RA * DT) > 1 ? 128 / (RA * DT) : 1;
+#pragma unroll QK_UNROLL
         for (int d = 0; d < DP; ++d) {
             float qr[RA];
             load_rows<RA>(sQt + d * LDQ + RA * ty, qr);
-            const float4 kb = *reinterpret_cast<const float4*>(sKt + d * LDK + 4 * tx);
-            const float kk[4] = {kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
-            for (int a = 0; a < RA; ++a)
+            for (int qq = 0; qq < KQ; ++qq) {
+                const float4 kb = *reinterpret_cast<const float4*>(sKt + d * LDK + 64 * qq + 4 * tx);
+                const float kk[4] = {kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
-                for (int b = 0; b < 4; ++b) sc[a][b] = fmaf(qr[a], kk[b], sc[a][b]);
+                for (int a = 0; a < RA; ++a)
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) sc[a][4 * qq + b] = fmaf(qr[a], kk[b], sc[a][4 * qq + b]);
+            }
         }
         float alpha[RA];
         // Tiles wholly inside the key range and (causal) wholly at or below the diagonal need no mask.
-        const bool masked = n0 + FA_BC > k_end || (causal && n0 + FA_BC - 1 > m0);
+        const bool masked = n0 + BC > k_end || (causal && n0 + BC - 1 > m0);
 #pragma unroll
         for (int a = 0; a < RA; ++a) {
             const int row = m0 + RA * ty + a;
             float mx = -INFINITY;
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int key = n0 + 4 * tx + b;
+            for (int t = 0; t < NK; ++t) {
+                const int key = n0 + 64 * (t >> 2) + 4 * tx + (t & 3);
                 const bool valid = !masked || (key < k_end && !(causal && key > row));
-                sc[a][b] = valid ? sc[a][b] * scale_log2 : -INFINITY;
-                mx = fmaxf(mx, sc[a][b]);
+                sc[a][t] = valid ? sc[a][t] * scale_log2 : -INFINITY;
+                mx = fmaxf(mx, sc[a][t]);
             }
 #pragma unroll
             for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
             const float m_new = fmaxf(m_run[a], mx);
             // Rows with nothing visible yet keep m_new = -inf; shift by 0 so exp2 stays finite.
             const float m_use = m_new == -INFINITY ? 0.0f : m_new;
-            alpha[a] = exp2f(m_run[a] - m_use);
+            alpha[a] = fast_exp2(m_run[a] - m_use);
             float psum = 0.0f;
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const float pb = exp2f(sc[a][b] - m_use);
-                psum += pb;
-                sc[a][b] = pb;
+            for (int t = 0; t < NK; ++t) {
+                const float pt = fast_exp2(sc[a][t] - m_use);
+                psum += pt;
+                sc[a][t] = pt;
             }
 #pragma unroll
             for (int off = 1; off < 16; off <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
             l_run[a] = l_run[a] * alpha[a] + psum;
             m_run[a] = m_new;
         }
-        // P transposed: key 4tx+b, this thread's RA consecutive rows as one vector store.
+        // P transposed: key 64q + 4tx + b, this thread's RA consecutive rows as vector stores.
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            float* dst = sP + (4 * tx + b) * LDP + RA * ty;
-            if constexpr (RA == 4) {
-                *reinterpret_cast<float4*>(dst) = make_float4(sc[0][b], sc[1][b], sc[2][b], sc[3][b]);
-            } else if constexpr (RA == 2) {
-                *reinterpret_cast<float2*>(dst) = make_float2(sc[0][b], sc[1][b]);
-            } else {
-                dst[0] = sc[0][b];
-            }
+        for (int t = 0; t < NK; ++t) {
+            float col_p[RA];
+#pragma unroll
+            for (int a = 0; a < RA; ++a) col_p[a] = sc[a][t];
+            store_rows<RA>(sP + (64 * (t >> 2) + 4 * tx + (t & 3)) * LDP + RA * ty, col_p);
         }
         __syncthreads();
 #pragma unroll
         for (int a = 0; a < RA; ++a)
 #pragma unroll
             for (int c = 0; c < DT; ++c) o[a][c] *= alpha[a];
-#pragma unroll 4
-        for (int j = 0; j < FA_BC; ++j) {
+#pragma unroll PV_UNROLL
+        for (int j = 0; j < BC; ++j) {
             float pv[RA];
             load_rows<RA>(sP + j * LDP + RA * ty, pv);
             if constexpr (L::VEC_COLS) {
@@ -562,7 +601,7 @@ __global__ void __launch_bounds__(256, 2) flash_attn_simt_kernel(T* __restrict__
         float lsum = 0.0f, osum = 0.0f;
         for (int t = 0; t < ns; ++t) {
             const float mt = *cluster.map_shared_rank(sM + r, t);
-            const float w = mt == -INFINITY ? 0.0f : exp2f(mt - mmax);
+            const float w = mt == -INFINITY ? 0.0f : fast_exp2(mt - mmax);
             lsum = fmaf(*cluster.map_shared_rank(sL + r, t), w, lsum);
             osum = fmaf(*cluster.map_shared_rank(sO + r * DP + d, t), w, osum);
         }
@@ -619,23 +658,23 @@ template cudaError_t conv2d_simt_launch<float>(float*, const float*, const float
 template cudaError_t conv2d_simt_launch<__nv_bfloat16>(float*, const __nv_bfloat16*, const __nv_bfloat16*, const float*,
                                                        const Conv2dShape&, cudaStream_t);
 
-template <typename T, int DT, int RA>
+template <typename T, int DT, int RA, int KQ>
 static cudaError_t flash_attn_simt_launch_ra(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
                                              int ns, cudaStream_t stream) {
-    using L = FaSmem<DT, RA>;
+    using L = FaCfg<DT, RA, KQ>;
     const size_t smem = sizeof(float) * L::floats;
     // fp32 planes with D % 4 == 0 and 16-byte aligned bases take the float4 tile loads.
     constexpr bool kF32 = sizeof(T) == 4;
     const bool vec = kF32 && D % 4 == 0 && ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                                              reinterpret_cast<uintptr_t>(v)) & 15u) == 0;
-    auto kernel = vec ? flash_attn_simt_kernel<T, DT, RA, kF32> : flash_attn_simt_kernel<T, DT, RA, false>;
+    auto kernel = vec ? flash_attn_simt_kernel<T, DT, RA, KQ, kF32> : flash_attn_simt_kernel<T, DT, RA, KQ, false>;
     static DeviceOnce attr_once[2];
     cudaError_t e = attr_once[vec ? 1 : 0].run([smem, kernel] {
         return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     });
     if (e != cudaSuccess) return e;
     const int q_tiles = (S + L::BR - 1) / L::BR;
-    const int key_split = ((S + ns - 1) / ns + FA_BC - 1) / FA_BC * FA_BC;
+    const int key_split = ((S + ns - 1) / ns + L::BC - 1) / L::BC * L::BC;
     const float scale_log2 = scale * 1.4426950408889634f;  // scores in the exp2 domain
     dim3 grid(static_cast<unsigned>(q_tiles * ns), static_cast<unsigned>(B * H));
     if (ns == 1) {
@@ -657,13 +696,15 @@ static cudaError_t flash_attn_simt_launch_ra(T* out, const T* q, const T* k, con
     return cudaLaunchKernelEx(&cfg, kernel, out, q, k, v, H, S, D, scale_log2, causal, key_split);
 }
 
+// Register tiles served: rows x keys per thread 1x4, 2x4 and 4x4. (An 8 x 8 tile, 128 x 128 per
+// CTA and one CTA per SM, measured no faster on C3: 32.8 vs 32.8 us with a 4-way split.)
 template <typename T, int DT>
 static cudaError_t flash_attn_simt_launch_dt(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
                                              int ra, int ns, cudaStream_t stream) {
     switch (ra) {
-        case 4: return flash_attn_simt_launch_ra<T, DT, 4>(out, q, k, v, B, H, S, D, scale, causal, ns, stream);
-        case 2: return flash_attn_simt_launch_ra<T, DT, 2>(out, q, k, v, B, H, S, D, scale, causal, ns, stream);
-        case 1: return flash_attn_simt_launch_ra<T, DT, 1>(out, q, k, v, B, H, S, D, scale, causal, ns, stream);
+        case 4: return flash_attn_simt_launch_ra<T, DT, 4, 1>(out, q, k, v, B, H, S, D, scale, causal, ns, stream);
+        case 2: return flash_attn_simt_launch_ra<T, DT, 2, 1>(out, q, k, v, B, H, S, D, scale, causal, ns, stream);
+        case 1: return flash_attn_simt_launch_ra<T, DT, 1, 1>(out, q, k, v, B, H, S, D, scale, causal, ns, stream);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -685,23 +726,24 @@ cudaError_t flash_attn_simt_launch_cfg(T* out, const T* q, const T* k, const T* 
     }
 }
 
-FlashSimtConfig flash_attn_simt_config(int B, int H, int S) {
-    // Rows per thread: 4 (64-row query tiles) when that gives at least one CTA per SM; else 2 when
-    // 32-row tiles fill half the SMs; else 1. Then, while fewer than 148 CTAs would run and each
-    // would walk more than one 64-key tile, the keys are split over 2, 4 or 8 CTAs of a cluster.
-    const long long bh = static_cast<long long>(B) * H;
-    FlashSimtConfig c{1, 1};
-    if ((S + 63) / 64 * bh >= 148) c.ra = 4;
-    else if ((S + 31) / 32 * bh >= 74) c.ra = 2;
-    const long long tiles = (S + 16 * c.ra - 1) / (16 * c.ra) * bh;
-    while (c.ns < 8 && tiles * c.ns < 148 && (S + c.ns - 1) / c.ns > FA_BC) c.ns *= 2;
+FlashSimtConfig flash_attn_simt_config(int B, int H, int S, int causal) {
+    // 64-row query tiles (4 rows per thread: 16 FMAs per pair of 16-byte shared loads) unless the
+    // sequence is short enough that most of such a tile would be padding. Then the keys of each
+    // query tile are split over 2, 4 or 8 CTAs of a cluster until the grid holds 1.5 CTAs per SM
+    // (3 for causal, whose early query tiles see few keys and whose empty splits end at once).
+    // Measured on B200, fp32, L2 flushed (us): 1x8x512x64 rows/thread x split 4x4 32.8 (2x1 47.1,
+    // 4x8 37.9); 1x4x300x40 causal 4x8 18.5 (2x1 26.6); 2x3x1000x64 causal 4x8 81.1 (2x1 113.0).
+    FlashSimtConfig c{S > 32 ? 4 : (S > 16 ? 2 : 1), 1};
+    const long long tiles = static_cast<long long>((S + 16 * c.ra - 1) / (16 * c.ra)) * B * H;
+    const long long want = 148LL * 3 / 2;
+    while (c.ns < 8 && tiles * c.ns < want * (causal ? 2 : 1)) c.ns *= 2;
     return c;
 }
 
 template <typename T>
 cudaError_t flash_attn_simt_launch(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
                                    cudaStream_t stream) {
-    const FlashSimtConfig c = flash_attn_simt_config(B, H, S);
+    const FlashSimtConfig c = flash_attn_simt_config(B, H, S, causal);
     return flash_attn_simt_launch_cfg(out, q, k, v, B, H, S, D, scale, causal, c.ra, c.ns, stream);
 }
 template cudaError_t flash_attn_simt_launch<float>(float*, const float*, const float*, const float*, int, int, int, int, float, int,

@@ -28,7 +28,7 @@ struct FlashSimtConfig {
     int ra;
     int ns;
 };
-FlashSimtConfig flash_attn_simt_config(int B, int H, int S);
+FlashSimtConfig flash_attn_simt_config(int B, int H, int S, int causal);
 template <typename T>
 cudaError_t flash_attn_simt_launch_cfg(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
                                        int ra, int ns, cudaStream_t stream);
