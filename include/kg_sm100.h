@@ -89,7 +89,8 @@ KG_API int kg_sm100_conv2d_entry(const KgArgSlot* ordered_args, unsigned long lo
 /* flash_attention_inputs_dynamic_tile_dynamic_kernel(out, q, k, v [B,H,S,D], br, bc[, scale, causal])
  * Replaces kernel/flash_attention/inputs_dynamic_tile_dynamic.py:96-195. With 6 slots the result is
  * the reference's softmax(q k^T) v; two optional trailing slots (extension) give the score scale
- * (float slot) and a causal flag (int slot). out has the dtype of q/k/v (f32 or bf16). */
+ * (float slot) and a causal flag (int slot). q/k/v are f32 or bf16; out is f32 (the reference's
+ * output type) or the inputs' dtype (see kg_sm100_flash_attention_ex for the bf16 -> f32 case). */
 KG_API int kg_sm100_flash_attention_entry(const KgArgSlot* ordered_args, unsigned long long arg_count);
 
 /* ---------------------------------------------------------------- cost capture */
@@ -148,6 +149,15 @@ KG_API int kg_sm100_conv2d(float* out, const void* input, const void* weight, in
 KG_API int kg_sm100_flash_attention(void* out, const void* q, const void* k, const void* v, int dtype,
                              long long B, long long H, long long S, long long D, float scale, int causal,
                              void* stream);
+
+/* The same with the output's dtype given apart from the inputs': `out_dtype` == `dtype`, or
+ * KG_DTYPE_F32 for bf16 inputs -- the reference's attention output is f32 whatever its inputs
+ * (kernel/flash_attention/inputs_dynamic_tile_dynamic.py:96-103). The f32 output of bf16 inputs is
+ * written by the tensor-core kernel (head dim 64 or 128, positive scale, 16-byte aligned tensors);
+ * other cases return KG_ERR_UNSUPPORTED. The slot entry takes the output dtype from the `out` slot. */
+KG_API int kg_sm100_flash_attention_ex(void* out, int out_dtype, const void* q, const void* k, const void* v, int dtype,
+                                       long long B, long long H, long long S, long long D, float scale, int causal,
+                                       void* stream);
 
 /* Tensor-core conv2d that allocates nothing. No counterpart in the reference.
  *

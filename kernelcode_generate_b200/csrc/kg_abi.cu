@@ -330,9 +330,15 @@ int conv2d_shape(kg::Conv2dShape* s, long long B, long long C, long long XH, lon
     return KG_OK;
 }
 
-int flash_attention_impl(void* out, const void* q, const void* k, const void* v, int dtype, long long B, long long H, long long S,
-                         long long D, float scale, int causal, cudaStream_t stream) {
+// out_dtype: the output's type, `dtype` (the inputs') or, for bf16 inputs on the tensor-core path,
+// f32 (the reference's attention output is f32 whatever the inputs, inputs_dynamic_tile_dynamic.py:96-103).
+int flash_attention_impl(void* out, int out_dtype, const void* q, const void* k, const void* v, int dtype, long long B, long long H,
+                         long long S, long long D, float scale, int causal, cudaStream_t stream) {
     if (!out || !q || !k || !v) return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention: null pointer");
+    const bool f32_out_of_bf16 = dtype == KG_DTYPE_BF16 && out_dtype == KG_DTYPE_F32;
+    if (out_dtype != dtype && !f32_out_of_bf16)
+        return fail(KG_ERR_UNSUPPORTED, "flash_attention: output dtype %d with input dtype %d (f32 output of bf16 inputs, or equal dtypes)",
+                    out_dtype, dtype);
     if (B <= 0 || H <= 0 || S <= 0 || D <= 0) return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention: extents must be positive");
     if (B * H > 65535) return fail(KG_ERR_UNSUPPORTED, "flash_attention: B*H > 65535");
     if (S > 0x7fffffffLL || D > 128) return fail(KG_ERR_UNSUPPORTED, "flash_attention: head dim %lld > 128 not supported", D);
@@ -353,10 +359,13 @@ int flash_attention_impl(void* out, const void* q, const void* k, const void* v,
             (rc = make_tmap_3d_bf16(&tv, v, B * H, S, D, 128)))
             return rc;
         g_last_kernel = "flash_fwd_tc_kernel";
-        KG_CUDA_TRY(kg::flash_fwd_tc_launch(tq, tk, tv, static_cast<__nv_bfloat16*>(out), (int)(B * H), (int)S, (int)D, scale, causal,
+        KG_CUDA_TRY(kg::flash_fwd_tc_launch(tq, tk, tv, out, f32_out_of_bf16 ? 1 : 0, (int)(B * H), (int)S, (int)D, scale, causal,
                                             dev->status, stream));
         return KG_OK;
     }
+    if (f32_out_of_bf16)
+        return fail(KG_ERR_UNSUPPORTED, "flash_attention: an f32 output of bf16 inputs needs the tensor-core path (head dim 64 or 128, "
+                                        "positive scale, 16-byte aligned tensors; got D=%lld)", D);
     if (dtype == KG_DTYPE_BF16) {
         g_last_kernel = "flash_attn_simt_kernel<bf16>";
         KG_CUDA_TRY(kg::flash_attn_simt_launch(static_cast<__nv_bfloat16*>(out), static_cast<const __nv_bfloat16*>(q),
@@ -698,7 +707,12 @@ int kg_sm100_conv2d(float* out, const void* input, const void* weight, int in_dt
 
 int kg_sm100_flash_attention(void* out, const void* q, const void* k, const void* v, int dtype, long long B, long long H, long long S,
                              long long D, float scale, int causal, void* stream) {
-    return flash_attention_impl(out, q, k, v, dtype, B, H, S, D, scale, causal, static_cast<cudaStream_t>(stream));
+    return flash_attention_impl(out, dtype, q, k, v, dtype, B, H, S, D, scale, causal, static_cast<cudaStream_t>(stream));
+}
+
+int kg_sm100_flash_attention_ex(void* out, int out_dtype, const void* q, const void* k, const void* v, int dtype, long long B, long long H,
+                                long long S, long long D, float scale, int causal, void* stream) {
+    return flash_attention_impl(out, out_dtype, q, k, v, dtype, B, H, S, D, scale, causal, static_cast<cudaStream_t>(stream));
 }
 
 // Slots: (out[H,W] f32, lhs[H,K], rhs[K,W], bias[W] | absent, tile_h, tile_w, tile_k).
@@ -820,29 +834,32 @@ int kg_sm100_flash_attention_entry(const KgArgSlot* slots, unsigned long long n)
         if (q.shape[d] != out.shape[d] || k.shape[d] != out.shape[d] || v.shape[d] != out.shape[d])
             return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention: out/q/k/v shapes differ");
     }
-    if (q.dtype != k.dtype || q.dtype != v.dtype || q.dtype != out.dtype)
-        return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention: out/q/k/v dtypes differ");
+    if (q.dtype != k.dtype || q.dtype != v.dtype)
+        return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention: q/k/v dtypes differ");
+    if (out.dtype != q.dtype && !(q.dtype == KG_DTYPE_BF16 && out.dtype == KG_DTYPE_F32))
+        return fail(KG_ERR_INVALID_ARGUMENT, "flash_attention: out must be f32 or the inputs' dtype");
     std::lock_guard<std::mutex> call_lock(g_call_mu);
     cudaStream_t stream = 0;
     std::vector<MemArg*> all = {&out, &q, &k, &v};
     if ((rc = stage_alloc(all))) return rc;
     const long long BH = out.shape[0] * out.shape[1], S = out.shape[2], D = out.shape[3];
     cost_work((causal ? 2.0 : 4.0) * BH * S * S * D, all);  // causal: the causal-half count
-    const size_t plane = static_cast<size_t>(S) * D * (q.dtype == KG_DTYPE_BF16 ? 2 : 4);  // one (b, h)
+    const size_t plane = static_cast<size_t>(S) * D * dtype_size(q.dtype);        // one (b, h) of an input
+    const size_t out_plane = static_cast<size_t>(S) * D * dtype_size(out.dtype);  // one (b, h) of the output
     const std::vector<RowArg> in = {{&q, plane}, {&k, plane}, {&v, plane}};
-    const RowArg out_rows = {&out, plane};
+    const RowArg out_rows = {&out, out_plane};
     if (pipeline_worth_it(in, out_rows, BH)) {
         return run_row_blocks(BH, (BH + 7) / 8, {}, in, out_rows, [&](long long h0, long long h1, cudaStream_t st) {
             const size_t off = static_cast<size_t>(h0) * plane;
-            return flash_attention_impl(static_cast<char*>(out.dev) + off, static_cast<const char*>(q.dev) + off,
-                                        static_cast<const char*>(k.dev) + off, static_cast<const char*>(v.dev) + off, q.dtype, 1, h1 - h0, S, D,
-                                        scale, causal, st);
+            return flash_attention_impl(static_cast<char*>(out.dev) + static_cast<size_t>(h0) * out_plane, out.dtype,
+                                        static_cast<const char*>(q.dev) + off, static_cast<const char*>(k.dev) + off,
+                                        static_cast<const char*>(v.dev) + off, q.dtype, 1, h1 - h0, S, D, scale, causal, st);
         });
     }
     if ((rc = upload_all_but_out(all, stream))) return rc;
     rc = cost_timed(stream, [&] {
-        return flash_attention_impl(out.dev, q.dev, k.dev, v.dev, q.dtype, out.shape[0], out.shape[1], out.shape[2], out.shape[3], scale,
-                                    causal, stream);
+        return flash_attention_impl(out.dev, out.dtype, q.dev, k.dev, v.dev, q.dtype, out.shape[0], out.shape[1], out.shape[2], out.shape[3],
+                                    scale, causal, stream);
     });
     return finish_call(rc, &out, stream);
 }

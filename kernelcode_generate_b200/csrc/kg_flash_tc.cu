@@ -112,10 +112,12 @@ __device__ __forceinline__ int key_tiles_for(int q0, int S, int causal) {
     return (last_key + BN - 1) / BN;
 }
 
-template <int D>
+// OUT_F32: the output is f32 (the reference's `out` type for attention, whatever the input type)
+// instead of the inputs' bf16.
+template <int D, bool OUT_F32>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, __nv_bfloat16* __restrict__ out, int S, float scale_log2,
+                        const __grid_constant__ CUtensorMap tm_v, void* __restrict__ out, int S, float scale_log2,
                         int causal, int num_pairs, int BH, int group_heads, int* status) {
     using Cfg = FlashCfg<D>;
     extern __shared__ uint8_t smem_raw[];
@@ -410,26 +412,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             unpack_f32x2(add_f32x2(add_f32x2(sum2[0], sum2[1]), add_f32x2(sum2[2], sum2[3])), sum_lo, sum_hi);
             l_run = l_run * alpha + (sum_lo + sum_hi);
         }
-        // epilogue: O / l -> bf16 -> global
+        // epilogue: O / l -> bf16 (or f32) -> global
         if (n > 0 && !warp_aborted(abort)) {
             if (warp_all(mbar_wait(&bars->o_done[i], 0, abort, status, kDevTimeoutEpilogue))) {
                 tc_fence_after();
                 const float inv = 1.0f / l_run;
-                __nv_bfloat16* dst = out + (static_cast<size_t>(bh) * S + row) * D;
+                const size_t row_off = (static_cast<size_t>(bh) * S + row) * D;
 #pragma unroll 1
                 for (int c = 0; c < D / 32; ++c) {
                     uint32_t v[32];
                     tmem_ld_32x32b_x32(o_addr + c * 32, v);
                     tmem_wait_ld();
                     if (row < S) {
-                        uint4 pk[4];
-                        uint32_t* w = reinterpret_cast<uint32_t*>(pk);
+                        if constexpr (OUT_F32) {
+                            float4* d4 = reinterpret_cast<float4*>(static_cast<float*>(out) + row_off + c * 32);
 #pragma unroll
-                        for (int t = 0; t < 16; ++t)
-                            w[t] = pack_bf16(__uint_as_float(v[2 * t]) * inv, __uint_as_float(v[2 * t + 1]) * inv);
-                        uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+                            for (int t = 0; t < 8; ++t)
+                                d4[t] = make_float4(__uint_as_float(v[4 * t]) * inv, __uint_as_float(v[4 * t + 1]) * inv,
+                                                    __uint_as_float(v[4 * t + 2]) * inv, __uint_as_float(v[4 * t + 3]) * inv);
+                        } else {
+                            uint4 pk[4];
+                            uint32_t* w = reinterpret_cast<uint32_t*>(pk);
 #pragma unroll
-                        for (int t = 0; t < 4; ++t) d4[t] = pk[t];
+                            for (int t = 0; t < 16; ++t)
+                                w[t] = pack_bf16(__uint_as_float(v[2 * t]) * inv, __uint_as_float(v[2 * t + 1]) * inv);
+                            uint4* d4 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + row_off + c * 32);
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) d4[t] = pk[t];
+                        }
                     }
                 }
             }
@@ -465,35 +475,33 @@ static int flash_group_heads(int BH, int S, int D) {
 // compiled register count. The warpgroups' setmaxnreg budgets assume LAUNCH_REGS registers per
 // thread at launch; with fewer, the softmax warpgroups' increase could never be granted, so the
 // launch is refused.
-template <int D>
+template <int D, bool OUT_F32>
 static cudaError_t flash_fwd_tc_setup() {
-    cudaError_t e = cudaFuncSetAttribute(flash_fwd_tc_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FlashCfg<D>::SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(flash_fwd_tc_kernel<D, OUT_F32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)FlashCfg<D>::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     cudaFuncAttributes fa{};
-    if ((e = cudaFuncGetAttributes(&fa, flash_fwd_tc_kernel<D>)) != cudaSuccess) return e;
+    if ((e = cudaFuncGetAttributes(&fa, flash_fwd_tc_kernel<D, OUT_F32>)) != cudaSuccess) return e;
     return fa.numRegs == LAUNCH_REGS ? cudaSuccess : cudaErrorInvalidConfiguration;
 }
 
 size_t flash_fwd_tc_smem_bytes(int D) { return D == 64 ? FlashCfg<64>::SMEM_BYTES : FlashCfg<128>::SMEM_BYTES; }
 
-cudaError_t flash_fwd_tc_launch(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v, __nv_bfloat16* out,
+cudaError_t flash_fwd_tc_launch(const CUtensorMap& tm_q, const CUtensorMap& tm_k, const CUtensorMap& tm_v, void* out, int out_f32,
                                 int BH, int S, int D, float scale, int causal, int* status, cudaStream_t stream) {
     const int num_pairs = (S + 2 * BM - 1) / (2 * BM);
     const float scale_log2 = scale * 1.4426950408889634f;
     const int group_heads = flash_group_heads(BH, S, D);
     dim3 grid(static_cast<unsigned>(num_pairs) * static_cast<unsigned>(BH));
-    static DeviceOnce attr_once[2];
-    const cudaError_t e = D == 64 ? attr_once[0].run(flash_fwd_tc_setup<64>) : attr_once[1].run(flash_fwd_tc_setup<128>);
+    if (D != 64 && D != 128) return cudaErrorInvalidValue;
+    static DeviceOnce attr_once[4];
+    const cudaError_t e = D == 64 ? (out_f32 ? attr_once[1].run(flash_fwd_tc_setup<64, true>) : attr_once[0].run(flash_fwd_tc_setup<64, false>))
+                                  : (out_f32 ? attr_once[3].run(flash_fwd_tc_setup<128, true>) : attr_once[2].run(flash_fwd_tc_setup<128, false>));
     if (e != cudaSuccess) return e;
-    if (D == 64) {
-        flash_fwd_tc_kernel<64><<<grid, NUM_THREADS, FlashCfg<64>::SMEM_BYTES, stream>>>(tm_q, tm_k, tm_v, out, S, scale_log2, causal,
-                                                                                         num_pairs, BH, group_heads, status);
-    } else if (D == 128) {
-        flash_fwd_tc_kernel<128><<<grid, NUM_THREADS, FlashCfg<128>::SMEM_BYTES, stream>>>(tm_q, tm_k, tm_v, out, S, scale_log2,
-                                                                                           causal, num_pairs, BH, group_heads, status);
-    } else {
-        return cudaErrorInvalidValue;
-    }
+    auto kernel = D == 64 ? (out_f32 ? flash_fwd_tc_kernel<64, true> : flash_fwd_tc_kernel<64, false>)
+                          : (out_f32 ? flash_fwd_tc_kernel<128, true> : flash_fwd_tc_kernel<128, false>);
+    kernel<<<grid, NUM_THREADS, flash_fwd_tc_smem_bytes(D), stream>>>(tm_q, tm_k, tm_v, out, S, scale_log2, causal, num_pairs, BH, group_heads,
+                                                                     status);
     return cudaGetLastError();
 }
 

@@ -90,9 +90,10 @@ def conv2d(out, x, w, bias=None, stride=(1, 1), dilation=(1, 1), pads=(0, 0, 0, 
 
 
 def flash_attention(out, q, k, v, scale=1.0, causal=False, stream=None):
-    """out = softmax(q k^T * scale [causal]) v over [B,H,S,D]; all tensors share one dtype."""
+    """out = softmax(q k^T * scale [causal]) v over [B,H,S,D]; q/k/v share one dtype, out has it
+    too or is f32 (the reference's output type) for bf16 inputs."""
     _check_cuda(out, q, k, v)
     B, H, S, D = q.shape
-    runtime.check(runtime.load().kg_sm100_flash_attention(out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), _dtype(q),
-                                                          B, H, S, D, float(scale), int(bool(causal)), _stream(stream)))
+    runtime.check(runtime.load().kg_sm100_flash_attention_ex(out.data_ptr(), _dtype(out), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                                             _dtype(q), B, H, S, D, float(scale), int(bool(causal)), _stream(stream)))
     return out

@@ -33,6 +33,7 @@ EXPORTED_SYMBOLS = (
     "kg_sm100_matmul",
     "kg_sm100_conv2d",
     "kg_sm100_flash_attention",
+    "kg_sm100_flash_attention_ex",
     "kg_sm100_device_status",
     "kg_sm100_last_error",
     "kg_sm100_last_kernel",
@@ -97,6 +98,9 @@ def load() -> ctypes.CDLL:
     lib.kg_sm100_conv2d.restype = ctypes.c_int
     lib.kg_sm100_flash_attention.argtypes = [_VP, _VP, _VP, _VP, ctypes.c_int, _LL, _LL, _LL, _LL, ctypes.c_float, ctypes.c_int, _VP]
     lib.kg_sm100_flash_attention.restype = ctypes.c_int
+    lib.kg_sm100_flash_attention_ex.argtypes = [_VP, ctypes.c_int, _VP, _VP, _VP, ctypes.c_int, _LL, _LL, _LL, _LL, ctypes.c_float,
+                                                ctypes.c_int, _VP]
+    lib.kg_sm100_flash_attention_ex.restype = ctypes.c_int
     lib.kg_sm100_device_status.argtypes = [ctypes.POINTER(ctypes.c_int)]
     lib.kg_sm100_device_status.restype = ctypes.c_int
     lib.kg_sm100_last_error.argtypes = []

@@ -11,6 +11,7 @@
 from __future__ import annotations
 
 import math
+import os
 
 import numpy as np
 import pytest
@@ -170,6 +171,12 @@ def test_c4_full_size_sampled_rows(cuda_device):
         rows = (r0, r0 + 4)
         expect = oracle.matmul(inp["lhs"], inp["rhs"], tiles=cfg.tiles, rows=rows)
         np.testing.assert_allclose(host[r0:r0 + 4], expect[r0:r0 + 4], **BF16_TOL)
+    # one whole 256-row pair-tile band in the middle (both 256-column halves of every 512-wide
+    # tile, all 16 column tiles), against the reference's own helpers where they are built
+    impl = "ref" if oracle.ref_available("O2") else "port"
+    band = (4352, 4608)
+    expect = oracle.matmul(inp["lhs"], inp["rhs"], tiles=(64, 96, 72), rows=band, impl=impl, threads=os.cpu_count() or 1)
+    np.testing.assert_allclose(host[band[0]:band[1]], expect[band[0]:band[1]], **BF16_TOL)
     # size-independent property: ones^T (A B) == (ones^T A) B, in fp64 on the GPU
     lhs_sum = a.double().sum(0)
     expect_colsum = (lhs_sum @ b.double()).cpu().numpy()
@@ -460,6 +467,13 @@ def test_c5_full_size_sampled_rows(cuda_device):
                                             bh=(bh, bh + 1), q_rows=(q0, q1))
             got = host.reshape(-1, s["S"], s["D"])[bh, q0:q1]
             np.testing.assert_allclose(got, expect.reshape(-1, s["S"], s["D"])[bh, q0:q1], **BF16_TOL)
+    # one whole (b, h) plane from a middle group of heads: all 8192 query rows, all 32 query-tile
+    # pairs and the causal diagonal of every key tile
+    impl = "ref" if oracle.ref_available("O2") else "port"
+    bh = 70
+    expect = oracle.flash_attention(inp["q"], inp["k"], inp["v"], tiles=cfg.tiles, scale=s["scale"], causal=True, bh=(bh, bh + 1),
+                                    impl=impl, threads=os.cpu_count() or 1)
+    np.testing.assert_allclose(host.reshape(-1, s["S"], s["D"])[bh], expect.reshape(-1, s["S"], s["D"])[bh], **BF16_TOL)
     vf = v.float()
     vmax = vf.amax(dim=2, keepdim=True)
     vmin = vf.amin(dim=2, keepdim=True)
@@ -600,3 +614,54 @@ def test_engine_execute_on_a_stream_matches_the_synchronous_entry(cuda_device):
     cv.execute(args=(cgot, x, w, None, 1, 1, 1, 1, 1, 1, 1, 1, 8, 16, 4, 8, 9), stream=side)
     side.synchronize()
     assert torch.equal(cref, cgot)
+
+
+# ---------------------------------------------------------------- f32 output of bf16 attention
+BF16_FLASH = [c for c in CASES if c[1] == "flash_attention" and c[3]["q"].dtype == np.uint16]
+
+
+@pytest.mark.parametrize("name,kind,params,inputs", BF16_FLASH, ids=[c[0] for c in BF16_FLASH])
+@pytest.mark.parametrize("memory", ["host", "device"])
+def test_bf16_attention_with_the_references_f32_output(cuda_device, name, kind, params, inputs, memory):
+    """The reference's attention output is f32 whatever its inputs: bf16 q/k/v with an f32 `out`
+    slot run on the tensor cores and match the golden output (fp32 maths on the bf16 inputs)."""
+    torch = _torch()
+    gold = load_golden(name)["expected"]
+    if memory == "host":
+        out = np.full(gold.shape, np.nan, np.float32)
+        args = {n: _host(inputs[n]) for n in ("q", "k", "v")}
+    else:
+        out = torch.full(gold.shape, float("nan"), device=cuda_device)
+        args = {n: _to_torch(inputs[n], cuda_device) for n in ("q", "k", "v")}
+    kernel = ExecutionEngine(target="cuda_sm100").compile(function=WRAPPER[kind])
+    kernel.execute(args=_slot_args(kind, params, args, out))
+    got = out if memory == "host" else out.cpu().numpy()
+    np.testing.assert_allclose(got, gold, **BF16_TOL)
+    assert runtime.last_kernel() == "flash_fwd_tc_kernel"
+
+
+@pytest.mark.parametrize("S,D,causal", [(300, 128, True), (1024, 64, False)])
+def test_bf16_attention_f32_output_equals_bf16_output_before_rounding(cuda_device, S, D, causal):
+    torch = _torch()
+    rng = np.random.default_rng(S + D)
+    shape = (2, 3, S, D)
+    q, k, v = (_to_torch(workloads.bf16_bits(rng.standard_normal(shape, dtype=np.float32)), cuda_device) for _ in range(3))
+    o16 = torch.empty(shape, dtype=torch.bfloat16, device=cuda_device)
+    o32 = torch.empty(shape, dtype=torch.float32, device=cuda_device)
+    kernels.flash_attention(o16, q, k, v, 1 / math.sqrt(D), causal)
+    kernels.flash_attention(o32, q, k, v, 1 / math.sqrt(D), causal)
+    torch.cuda.synchronize()
+    # the bf16 output is the f32 one rounded to bf16, bit for bit
+    assert torch.equal(o32.to(torch.bfloat16), o16)
+    expect = oracle.flash_attention(*(workloads.bf16_bits(x.float().cpu().numpy()) for x in (q, k, v)), tiles=(128, 128),
+                                    scale=1 / math.sqrt(D), causal=causal)
+    np.testing.assert_allclose(o32.cpu().numpy(), expect, **BF16_TOL)
+
+
+def test_bf16_attention_f32_output_needs_the_tensor_core_path(cuda_device):
+    torch = _torch()
+    q = torch.zeros((1, 2, 64, 40), dtype=torch.bfloat16, device=cuda_device)  # head dim 40: the CUDA-core fallback
+    out = torch.zeros((1, 2, 64, 40), dtype=torch.float32, device=cuda_device)
+    with pytest.raises(runtime.KernelError) as err:
+        kernels.flash_attention(out, q, q, q, 0.125, False)
+    assert err.value.code == runtime.KG_ERR_UNSUPPORTED and "tensor-core path" in str(err.value)
