@@ -220,7 +220,9 @@ int matmul_impl(float* out, const void* lhs, const void* rhs, int in_dtype, cons
             if (rc != KG_OK) return rc;
             if (M >= 256 && N >= 256 && dev->num_sms >= 2) {
                 const int block_n = kg::gemm_bf16_tc_pair_block_n((int)M, (int)N, dev->num_sms);
-                g_last_kernel = block_n == 512 ? "gemm_bf16_tc_pair_kernel<512>" : "gemm_bf16_tc_pair_kernel<256>";
+                g_last_kernel = block_n == 512   ? "gemm_bf16_tc_pair_kernel<512>"
+                                : block_n == 480 ? "gemm_bf16_tc_pair_kernel<480>"
+                                                 : "gemm_bf16_tc_pair_kernel<256>";
                 CUtensorMap tc;
                 const bool tma_out = N % 4 == 0 && aligned16(out);
                 if (tma_out && (rc = make_tmap_out_f32(&tc, out, M, N)) != KG_OK) return rc;

@@ -10,7 +10,7 @@ bool gemm_bf16_tc_supported(long long M, long long N, long long K);
 // tm_a: lhs [M,K] bf16, box 64(K) x 128(M), 128B swizzle. tm_b: rhs [K,N] bf16, box 64(N) x 64(K), 128B swizzle.
 cudaError_t gemm_bf16_tc_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_b, float* out, const float* bias, int M, int N,
                                 int K, int num_sms, int* status, cudaStream_t stream);
-// CTA-pair variant (kg_gemm_tc2.cu): 256x256 or 256x512 tiles (block_n), same tensor maps as above.
+// CTA-pair variant (kg_gemm_tc2.cu): 256x256, 256x480 or 256x512 tiles (block_n), same tensor maps as above.
 // Needs M, N >= 256.
 size_t gemm_bf16_tc_pair_smem_bytes();
 cudaError_t gemm_bf16_tc_pair_launch(const CUtensorMap& tm_a, const CUtensorMap& tm_b, float* out, const float* bias, int M, int N,

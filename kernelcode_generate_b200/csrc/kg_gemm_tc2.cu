@@ -1,4 +1,4 @@
-// bf16 x bf16 -> f32 GEMM on CTA pairs (tcgen05.mma.cta_group::2): 256 x 256 or 256 x 512 output tiles.
+// bf16 x bf16 -> f32 GEMM on CTA pairs (tcgen05.mma.cta_group::2): 256 x 256, 256 x 480 or 256 x 512 output tiles.
 //
 // Same contract as kg_gemm_tc.cu (the reference matmul loop nest,
 // kernel/matmul/inputs_dynamic_tile_dynamic.py:84-113): out[M,N] = lhs[M,K] . rhs[K,N] (+ bias[N]).
@@ -16,7 +16,9 @@
 // k-slice into one 512-column TMEM accumulator: 48 KB of A and B per CTA per k-step feed twice the
 // MMA work of the 256 x 256 tile's 32 KB. A quarter less L2 -> SM and DRAM traffic draws less
 // power, so under the 1 kW cap the SMs hold a higher clock; the price is a single accumulator, so
-// each tile's epilogue is not overlapped with MMAs. gemm_bf16_tc_pair_block_n picks the width.
+// each tile's epilogue is not overlapped with MMAs. The 256 x 480 tile (MMAs of 256 and 224
+// columns) fills more pairs in one wave where 512 would leave some idle. gemm_bf16_tc_pair_block_n
+// picks the width.
 #include "kg_gemm_tc.h"
 #include "kg_device_once.h"
 #include "kg_ptx.cuh"
@@ -39,15 +41,18 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t IDESC = idesc_f16(PBM, 256, true, true, false, true);  // one 256 x 256 x 16 MMA
 constexpr uint16_t PAIR_MASK = 0x3;
 
-// Pair tile of 256 x PBN (PBN = 256 or 512) as PBN / 256 halves of 256 columns. Per CTA and k-step:
-// A 128 x 64 and B 64 x (128 per half).
+// Pair tile of 256 x PBN (PBN = 256, 480 or 512) as halves of up to 256 columns, one MMA each per
+// 16-deep k-slice: 256 | 256 + 256 | 256 + 224. Per CTA and k-step: A 128 x 64 and B 64 x (half of
+// each MMA's columns, loaded as two 64-column boxes; the 224-column MMA reads 112 of its 128).
 template <int PBN>
 struct PairCfg {
-    static constexpr int HALVES = PBN / 256;
+    static constexpr int HALVES = (PBN + 255) / 256;
     static constexpr int STAGES = HALVES == 1 ? 6 : 4;
     static constexpr int NACC = HALVES == 1 ? 2 : 1;  // TMEM accumulators of PBN columns
     static constexpr uint32_t B_STAGE_BYTES = HALVES * 2 * B_BOX_BYTES;
-    static_assert((PBN == 256 || PBN == 512) && STAGES <= MAX_STAGES && NACC * PBN <= static_cast<int>(TMEM_COLS), "pair tile");
+    static constexpr int N_LAST = PBN - 256 * (HALVES - 1);  // columns of the last half's MMA
+    static constexpr uint32_t IDESC_LAST = idesc_f16(PBM, N_LAST, true, true, false, true);
+    static_assert((PBN == 256 || PBN == 512 || PBN == 480) && STAGES <= MAX_STAGES && NACC * PBN <= static_cast<int>(TMEM_COLS), "pair tile");
 };
 
 struct alignas(8) PairBarriers {
@@ -149,7 +154,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < 2 * HALVES; ++j)  // box j: half j / 2, this CTA's 128 columns of it
                         tma_load_2d_pair(b_dst + j * B_BOX_BYTES, &tm_b, leader_full,
-                                         nb * PBN + (j >> 1) * 256 + static_cast<int>(rank) * 128 + (j & 1) * 64, kb * BK);
+                                         nb * PBN + (j >> 1) * 256 + static_cast<int>(rank) * ((j >> 1) == HALVES - 1 ? PairCfg<PBN>::N_LAST / 2 : 128) + (j & 1) * 64,
+                                         kb * BK);
                     ++issued;
                     if (++stage == STAGES) {
                         stage = 0;
@@ -195,7 +201,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                             for (int h = 0; h < HALVES; ++h) {
                                 const uint64_t b_desc = smem_desc_sw128(b_base + h * 2 * B_BOX_BYTES + kk * 2048, B_BOX_BYTES, 1024);
-                                umma_f16_pair(d_tmem + h * 256, a_desc, b_desc, IDESC, (kb | kk) != 0 ? 1u : 0u);
+                                umma_f16_pair(d_tmem + h * 256, a_desc, b_desc, h == HALVES - 1 ? PairCfg<PBN>::IDESC_LAST : IDESC, (kb | kk) != 0 ? 1u : 0u);
                             }
                         }
                         umma_commit_pair_multicast(&bars->empty[stage], PAIR_MASK);
@@ -324,8 +330,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 
 size_t gemm_bf16_tc_pair_smem_bytes() { return pair_smem_bytes<256>(); }
 
-// 512 unless it costs more tile-columns on the busiest pair (waves x tile width) than 256: ragged
-// N (520 columns: two 512 tiles vs three 256) and grids under one wave of 256 tiles keep 256.
+// The width whose busiest pair has the fewest tile columns (waves x tile width). 480 takes grids
+// that one wave of 512-wide tiles leaves partly idle: the 1024-row shard of 8192^3 runs 72 tiles of
+// 480 on 74 pairs instead of 64 of 512 (86.1 vs 90.2 us; 168.0 vs 176.3 on 2048 rows). The full
+// 8192^3 keeps 512 (7 waves against 8). Ragged N (520 columns: two 512 tiles vs three 256) and
+// grids under one wave of 256 tiles keep 256.
 int gemm_bf16_tc_pair_block_n(int M, int N, int num_sms) {
     const long long pairs = num_sms / 2 > 0 ? num_sms / 2 : 1;
     const long long num_m = (M + PBM - 1) / PBM;
@@ -333,7 +342,9 @@ int gemm_bf16_tc_pair_block_n(int M, int N, int num_sms) {
         const long long tiles = num_m * ((N + pbn - 1) / pbn);
         return ((tiles + pairs - 1) / pairs) * pbn;
     };
-    return cost(512) <= cost(256) ? 512 : 256;
+    const long long c512 = cost(512), c480 = cost(480);
+    if (c480 < c512 && c480 < cost(256)) return 480;
+    return c512 <= cost(256) ? 512 : 256;
 }
 
 template <int PBN>
@@ -360,6 +371,7 @@ cudaError_t gemm_bf16_tc_pair_launch(const CUtensorMap& tm_a, const CUtensorMap&
                                      int num_sms, int* status, cudaStream_t stream, const CUtensorMap* tm_c, int block_n) {
     if (block_n == 256) return launch_pbn<256>(tm_a, tm_b, out, bias, M, N, K, num_sms, status, stream, tm_c);
     if (block_n == 512) return launch_pbn<512>(tm_a, tm_b, out, bias, M, N, K, num_sms, status, stream, tm_c);
+    if (block_n == 480) return launch_pbn<480>(tm_a, tm_b, out, bias, M, N, K, num_sms, status, stream, tm_c);
     return cudaErrorInvalidValue;
 }
 

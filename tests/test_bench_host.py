@@ -66,7 +66,7 @@ def test_a_shard_never_reports_the_full_problem_traffic():
         rows = bench.shard_range(8192, 0, world)
         shape = bench.launch_shape(c4, rows)
         assert shape == f"M{8192 // world}_N8192_K8192"
-        for label in (kernel, "gemm_bf16_tc_pair_kernel<256>"):
+        for label in (kernel, "gemm_bf16_tc_pair_kernel<256>", "gemm_bf16_tc_pair_kernel<480>"):
             t = bench.load_traffic(label, shape)
             assert t is None or t < full_bytes, (label, shape, t)
     c5 = workloads.ALL_CONFIGS["C5"]
@@ -75,11 +75,11 @@ def test_a_shard_never_reports_the_full_problem_traffic():
 
 def test_every_shard_launch_of_the_scaling_run_has_its_own_capture():
     """The N = 2 / 4 / 8 launches each have a capture of their own shape (the tile width the
-    library picks: 256 columns for 4096 rows, 512 for 2048 and 1024 rows), smaller than the full
+    library picks: 256 columns for 4096 rows, 480 for 2048 and 1024 rows), smaller than the full
     problem's, and C5's 16-plane shard at N = 8 too."""
     c4, c5 = workloads.ALL_CONFIGS["C4"], workloads.ALL_CONFIGS["C5"]
     full = bench.load_traffic("gemm_bf16_tc_pair_kernel<512>", "M8192_N8192_K8192")
-    for world, label in ((2, "gemm_bf16_tc_pair_kernel<256>"), (4, "gemm_bf16_tc_pair_kernel<512>"), (8, "gemm_bf16_tc_pair_kernel<512>")):
+    for world, label in ((2, "gemm_bf16_tc_pair_kernel<256>"), (4, "gemm_bf16_tc_pair_kernel<480>"), (8, "gemm_bf16_tc_pair_kernel<480>")):
         t = bench.load_traffic(label, bench.launch_shape(c4, bench.shard_range(8192, 0, world)))
         assert isinstance(t, int) and 0 < t < full, (world, t)
     t5 = bench.load_traffic("flash_fwd_tc_kernel", bench.launch_shape(c5, bench.shard_range(128, 0, 8)))

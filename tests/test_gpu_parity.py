@@ -185,17 +185,20 @@ def test_c4_full_size_sampled_rows(cuda_device):
 
 
 PAIR_256 = "gemm_bf16_tc_pair_kernel<256>"
+PAIR_480 = "gemm_bf16_tc_pair_kernel<480>"
 PAIR_512 = "gemm_bf16_tc_pair_kernel<512>"
 
 
-@pytest.mark.parametrize("M,K,N,with_bias,kernel", [(2000, 520, 2600, True, PAIR_512), (2048, 512, 2560, False, PAIR_512),
-                                                    (2048, 128, 2560, True, PAIR_512), (600, 1000, 8192, True, PAIR_512),
-                                                    (12600, 136, 696, True, PAIR_256), (18900, 72, 1000, False, PAIR_512)])
+@pytest.mark.parametrize("M,K,N,with_bias,kernel", [(2000, 520, 2600, True, PAIR_480), (2048, 512, 2560, False, PAIR_480),
+                                                    (2048, 128, 2560, True, PAIR_480), (600, 1000, 8192, True, PAIR_480),
+                                                    (12600, 136, 696, True, PAIR_256), (18900, 72, 1000, False, PAIR_512),
+                                                    (9400, 72, 1000, True, PAIR_512)])
 def test_bf16_gemm_pair_tiles_over_one_wave_vs_oracle(cuda_device, M, K, N, with_bias, kernel):
-    """Grids that need more than one wave of 256 x 256 pair tiles on 74 pairs (80-96 tiles, or one
-    wave of 40-48 256 x 512 tiles), three waves of 256 x 256 (150 tiles; 512 columns would waste a
-    third of the last n-block), two full waves of 256 x 512 (148 tiles); ragged M, N and K.
-    Whole result vs the oracle, and bitwise repeatable."""
+    """Grids that need more than one wave of 256 x 256 pair tiles on 74 pairs, run as one wave of
+    40-54 256 x 480 tiles (the second MMA of each k-slice 224 columns wide); three waves of 256 x 256
+    (150 tiles; wider tiles would waste a third of the last n-block); two full waves of 256 x 512
+    (148 tiles) and one full wave (74); ragged M, N and K. Whole result vs the oracle, and bitwise
+    repeatable."""
     torch = _torch()
     rng = np.random.default_rng(M + K + N)
     a = workloads.bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
@@ -239,8 +242,9 @@ def test_bf16_gemm_pair_unaligned_output_vs_oracle(cuda_device, with_bias):
 
 
 def test_c4_row_shard_of_eight(cuda_device):
-    """One rank's block of C4 at 8 GPUs (1024 x 8192 x 8192: 64 pair tiles of 256 x 512 on 74
-    pairs). Sampled rows vs the oracle and the column-sum identity over all rows."""
+    """One rank's block of C4 at 8 GPUs (1024 x 8192 x 8192: 72 pair tiles of 256 x 480 on 74
+    pairs, the last column of tiles 32 wide). Sampled rows vs the oracle and the column-sum
+    identity over all rows."""
     torch = _torch()
     rng = np.random.default_rng(8)
     M, K, N = 1024, 8192, 8192
@@ -250,7 +254,7 @@ def test_c4_row_shard_of_eight(cuda_device):
     out = torch.empty(M, N, device=cuda_device)
     kernels.matmul(out, a, b)
     torch.cuda.synchronize()
-    assert runtime.last_kernel() == PAIR_512
+    assert runtime.last_kernel() == PAIR_480
     assert runtime.device_status() == 0
     host = out.cpu().numpy()
     for r0 in (0, 251, 700, M - 4):
