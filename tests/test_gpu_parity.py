@@ -302,7 +302,7 @@ def test_host_buffer_matmul_row_blocks_match_device_path(cuda_device, M, with_bi
 
 @pytest.mark.parametrize("M,K,N,with_bias", [(3000, 1024, 3000, True), (4100, 2048, 1304, False)])
 def test_host_buffer_matmul_large_row_blocks_match_device_path(cuda_device, M, K, N, with_bias):
-    """Host lhs, rhs and out of 32 MiB and more, in row blocks of 512 or 768 rows with a ragged
+    """Host lhs, rhs and out of 32 MiB and more, in row blocks of 256 or 512 rows with a ragged
     last block, N not a multiple of 256; the result equals the one-launch device-buffer result
     bit for bit."""
     torch = _torch()
