@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstring>
 #include <functional>
+#include <algorithm>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -109,13 +110,14 @@ int get_encode_fn(EncodeTiledFn* fn) {
     return KG_OK;
 }
 
-// 2-D bf16 tensor map over a row-major [rows, cols] matrix, box {box_cols, box_rows}, 128B swizzle.
-int make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, int box_cols, int box_rows) {
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix whose rows are `pitch` elements apart
+// (0: cols, contiguous), box {box_cols, box_rows}, 128B swizzle.
+int make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, int box_cols, int box_rows, long long pitch = 0) {
     EncodeTiledFn encode = nullptr;
     int rc = get_encode_fn(&encode);
     if (rc != KG_OK) return rc;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch > 0 ? pitch : cols) * 2};
     cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
     cuuint32_t estrides[2] = {1, 1};
     CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estrides,
@@ -129,14 +131,15 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long rows, long l
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// 2-D f32 tensor map over a contiguous [rows, cols] matrix (dims {cols, rows}), box {32, 32}, 128B
-// swizzle (a box row is 128 bytes): the GEMM epilogue's TMA stores.
-int make_tmap_out_f32(CUtensorMap* map, void* base, long long rows, long long cols) {
+// 2-D f32 tensor map over a [rows, cols] matrix with rows `pitch` elements apart (0: contiguous),
+// dims {cols, rows}, box {32, 32}, 128B swizzle (a box row is 128 bytes): the GEMM epilogue's TMA
+// stores, which drop whatever falls outside the dims.
+int make_tmap_out_f32(CUtensorMap* map, void* base, long long rows, long long cols, long long pitch = 0) {
     EncodeTiledFn encode = nullptr;
     int rc = get_encode_fn(&encode);
     if (rc != KG_OK) return rc;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch > 0 ? pitch : cols) * 4};
     cuuint32_t box[2] = {32, 32};
     cuuint32_t estrides[2] = {1, 1};
     CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, estrides, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -246,6 +249,31 @@ int matmul_impl(float* out, const void* lhs, const void* rhs, int in_dtype, cons
         return KG_OK;
     }
     return fail(KG_ERR_UNSUPPORTED, "matmul: input dtype code %d not supported (f32=1, bf16=5)", in_dtype);
+}
+
+// One tensor-core launch on a column block of a wider matrix: out[M, N] (rows ldc floats apart) =
+// lhs[M, K] (contiguous) . rhs[K, N] (rows ldb elements apart) (+ bias[N]). Only the CTA-pair kernel
+// with its TMA-store epilogue runs here: its output goes through the tensor map, which carries the
+// pitch. Callers check matmul_tile_ok first.
+bool matmul_tile_ok(const void* out, long long ldc, const void* lhs, const void* rhs, long long ldb, long long M, long long K, long long N) {
+    return M >= 256 && N >= 256 && kg::gemm_bf16_tc_supported(M, N, K) && ldb % 8 == 0 && ldc % 4 == 0 && aligned16(out) && aligned16(lhs) &&
+           aligned16(rhs) && ldb < (1LL << 31) && ldc < (1LL << 31);
+}
+
+int matmul_tile(float* out, long long ldc, const void* lhs, const void* rhs, long long ldb, const float* bias, long long M, long long K,
+                long long N, cudaStream_t stream) {
+    DeviceInfo* dev = nullptr;
+    int rc = device_info(&dev);
+    if (rc != KG_OK) return rc;
+    if (dev->num_sms < 2 || !matmul_tile_ok(out, ldc, lhs, rhs, ldb, M, K, N)) return fail(KG_ERR_UNSUPPORTED, "matmul: column block not supported");
+    CUtensorMap ta, tb, tc;
+    if ((rc = make_tmap_2d_bf16(&ta, lhs, M, K, 64, kg::gemm_bf16_tc_tile_m())) != KG_OK) return rc;
+    if ((rc = make_tmap_2d_bf16(&tb, rhs, K, N, 64, 64, ldb)) != KG_OK) return rc;
+    if ((rc = make_tmap_out_f32(&tc, out, M, N, ldc)) != KG_OK) return rc;
+    const int block_n = kg::gemm_bf16_tc_pair_block_n((int)M, (int)N, dev->num_sms);
+    g_last_kernel = block_n == 512 ? "gemm_bf16_tc_pair_kernel<512>" : block_n == 480 ? "gemm_bf16_tc_pair_kernel<480>" : "gemm_bf16_tc_pair_kernel<256>";
+    KG_CUDA_TRY(kg::gemm_bf16_tc_pair_launch(ta, tb, out, bias, (int)M, (int)N, (int)K, dev->num_sms, dev->status, stream, &tc, block_n));
+    return KG_OK;
 }
 
 kg::ConvTcShape conv_tc_shape(const kg::Conv2dShape& s) {
@@ -537,10 +565,13 @@ int stage_alloc(std::vector<MemArg*>& args) {
 // kernels and downloads of successive row blocks overlap (the copy engines run both directions at
 // once while the GPU computes).
 constexpr int kPipeMaxChunks = 16;
+constexpr int kPipeMaxColBlocks = 4;
+constexpr int kPipeMaxTiles = kPipeMaxChunks * kPipeMaxColBlocks;
 struct Pipe {
     cudaStream_t up = nullptr, compute = nullptr, down = nullptr;
     cudaEvent_t uploaded[kPipeMaxChunks] = {};
-    cudaEvent_t computed[kPipeMaxChunks] = {};
+    cudaEvent_t uploaded_cols[kPipeMaxColBlocks] = {};
+    cudaEvent_t computed[kPipeMaxTiles] = {};
     cudaEvent_t operands = nullptr;
 };
 Pipe g_pipes[kg::kMaxDevices];
@@ -556,10 +587,9 @@ int get_pipe(Pipe** out) {
         KG_CUDA_TRY(cudaStreamCreateWithFlags(&p.compute, cudaStreamNonBlocking));
         KG_CUDA_TRY(cudaStreamCreateWithFlags(&p.down, cudaStreamNonBlocking));
         KG_CUDA_TRY(cudaEventCreateWithFlags(&p.operands, cudaEventDisableTiming));
-        for (int i = 0; i < kPipeMaxChunks; ++i) {
-            KG_CUDA_TRY(cudaEventCreateWithFlags(&p.uploaded[i], cudaEventDisableTiming));
-            KG_CUDA_TRY(cudaEventCreateWithFlags(&p.computed[i], cudaEventDisableTiming));
-        }
+        for (int i = 0; i < kPipeMaxChunks; ++i) KG_CUDA_TRY(cudaEventCreateWithFlags(&p.uploaded[i], cudaEventDisableTiming));
+        for (int i = 0; i < kPipeMaxColBlocks; ++i) KG_CUDA_TRY(cudaEventCreateWithFlags(&p.uploaded_cols[i], cudaEventDisableTiming));
+        for (int i = 0; i < kPipeMaxTiles; ++i) KG_CUDA_TRY(cudaEventCreateWithFlags(&p.computed[i], cudaEventDisableTiming));
     }
     *out = &p;
     return KG_OK;
@@ -642,6 +672,91 @@ int run_row_blocks(long long rows, long long block_rows, const std::vector<MemAr
     KG_CUDA_TRY(cudaStreamSynchronize(p->down));
     if (rc != KG_OK) return rc;
     MemArg done = *out.arg;
+    done.host = false;  // already downloaded; finish_call only checks the device status word
+    return finish_call(KG_OK, &done, p->down);
+}
+
+// Block boundaries over `total`: about `target` blocks, each a multiple of `grain` except the last,
+// none below `min_size` (a short remainder joins the block before it). Returns the block starts
+// plus `total`.
+std::vector<long long> block_bounds(long long total, int target, long long grain, long long min_size) {
+    long long size = (total + target - 1) / target;
+    size = (size + grain - 1) / grain * grain;
+    std::vector<long long> b;
+    for (long long x = 0; x < total; x += size) b.push_back(x);
+    if (b.size() > 1 && total - b.back() < min_size) b.pop_back();
+    b.push_back(total);
+    return b;
+}
+
+// Host-buffer bf16 matmul in row blocks of lhs and column blocks of rhs. Every output row needs all
+// of rhs, so with rhs uploaded whole the download direction idles for its whole upload (128 MiB,
+// 2.4 ms on 8192^3) before the first rows can come down. Here rhs goes up in column blocks
+// interleaved with lhs row blocks (B0, A0, A1, B1, A2, A3, B2, ...), and each output tile is
+// launched and downloaded as soon as its row block and column block have arrived, in that order.
+// Each output element is the same K-long sum, in the same order, as in a single launch, so the
+// result is the same bit for bit.
+int run_matmul_2d(MemArg& out, MemArg& lhs, MemArg& rhs, MemArg& bias, long long K, long long W, const std::vector<long long>& rows,
+                  const std::vector<long long>& cols) {
+    Pipe* p = nullptr;
+    int rc = get_pipe(&p);
+    if (rc != KG_OK) return rc;
+    const int nr = static_cast<int>(rows.size()) - 1, nc = static_cast<int>(cols.size()) - 1;
+    if (nr > kPipeMaxChunks || nc > kPipeMaxColBlocks) return fail(KG_ERR_UNSUPPORTED, "matmul: %d x %d blocks exceed the pipeline", nr, nc);
+    std::vector<std::pair<bool, int>> order = {{true, 0}};  // (column block of rhs?, index)
+    int next_row = 0;
+    for (int c = 1; c < nc; ++c) {
+        for (int k = 0; k < 2 && next_row < nr; ++k) order.push_back({false, next_row++});
+        order.push_back({true, c});
+    }
+    while (next_row < nr) order.push_back({false, next_row++});
+    std::vector<int> pos_row(nr), pos_col(nc);
+    for (int i = 0; i < static_cast<int>(order.size()); ++i) (order[i].first ? pos_col : pos_row)[order[i].second] = i;
+    const size_t b_pitch = static_cast<size_t>(W) * 2, a_row = static_cast<size_t>(K) * 2, c_pitch = static_cast<size_t>(W) * 4;
+    cost_mark_first(p->up);
+    if (bias.data != nullptr && bias.host) KG_CUDA_TRY(cudaMemcpyAsync(bias.dev, bias.data, bias.bytes, cudaMemcpyHostToDevice, p->up));
+    for (const auto& item : order) {
+        const int i = item.second;
+        if (item.first) {
+            const size_t off = static_cast<size_t>(cols[i]) * 2;
+            KG_CUDA_TRY(cudaMemcpy2DAsync(static_cast<char*>(rhs.dev) + off, b_pitch, static_cast<const char*>(rhs.data) + off, b_pitch,
+                                          static_cast<size_t>(cols[i + 1] - cols[i]) * 2, static_cast<size_t>(K), cudaMemcpyHostToDevice, p->up));
+            KG_CUDA_TRY(cudaEventRecord(p->uploaded_cols[i], p->up));
+        } else {
+            const size_t off = static_cast<size_t>(rows[i]) * a_row;
+            KG_CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(lhs.dev) + off, static_cast<const char*>(lhs.data) + off,
+                                        static_cast<size_t>(rows[i + 1] - rows[i]) * a_row, cudaMemcpyHostToDevice, p->up));
+            KG_CUDA_TRY(cudaEventRecord(p->uploaded[i], p->up));
+        }
+    }
+    std::vector<std::pair<int, int>> tiles;
+    for (int r = 0; r < nr; ++r)
+        for (int c = 0; c < nc; ++c) tiles.push_back({r, c});
+    std::stable_sort(tiles.begin(), tiles.end(), [&](const std::pair<int, int>& x, const std::pair<int, int>& y) {
+        return std::max(pos_row[x.first], pos_col[x.second]) < std::max(pos_row[y.first], pos_col[y.second]);
+    });
+    for (size_t t = 0; t < tiles.size() && rc == KG_OK; ++t) {
+        const int r = tiles[t].first, c = tiles[t].second;
+        const long long r0 = rows[r], r1 = rows[r + 1], c0 = cols[c], c1 = cols[c + 1];
+        KG_CUDA_TRY(cudaStreamWaitEvent(p->compute, p->uploaded[r], 0));
+        KG_CUDA_TRY(cudaStreamWaitEvent(p->compute, p->uploaded_cols[c], 0));
+        float* o = static_cast<float*>(out.dev) + static_cast<size_t>(r0) * W + c0;
+        rc = cost_timed(p->compute, [&] {
+            return matmul_tile(o, W, static_cast<const char*>(lhs.dev) + static_cast<size_t>(r0) * a_row,
+                               static_cast<const char*>(rhs.dev) + static_cast<size_t>(c0) * 2, W,
+                               bias.data != nullptr ? static_cast<const float*>(bias.dev) + c0 : nullptr, r1 - r0, K, c1 - c0, p->compute);
+        });
+        if (rc != KG_OK) break;
+        KG_CUDA_TRY(cudaEventRecord(p->computed[t], p->compute));
+        KG_CUDA_TRY(cudaStreamWaitEvent(p->down, p->computed[t], 0));
+        KG_CUDA_TRY(cudaMemcpy2DAsync(static_cast<float*>(out.data) + static_cast<size_t>(r0) * W + c0, c_pitch, o, c_pitch,
+                                      static_cast<size_t>(c1 - c0) * 4, static_cast<size_t>(r1 - r0), cudaMemcpyDeviceToHost, p->down));
+    }
+    KG_CUDA_TRY(cudaStreamSynchronize(p->up));
+    KG_CUDA_TRY(cudaStreamSynchronize(p->compute));
+    KG_CUDA_TRY(cudaStreamSynchronize(p->down));
+    if (rc != KG_OK) return rc;
+    MemArg done = out;
     done.host = false;  // already downloaded; finish_call only checks the device status word
     return finish_call(KG_OK, &done, p->down);
 }
@@ -746,6 +861,24 @@ int kg_sm100_matmul_entry(const KgArgSlot* slots, unsigned long long n) {
     const size_t esz = lhs.dtype == KG_DTYPE_BF16 ? 2 : 4;
     const std::vector<RowArg> in = {{&lhs, static_cast<size_t>(K) * esz}};
     const RowArg out_rows = {&out, static_cast<size_t>(W) * 4};
+    if (lhs.dtype == KG_DTYPE_BF16 && rhs.host && (bias.data == nullptr || bias.host) && H >= 2 * kPipeRowBlock && W >= 2048 &&
+        W % 8 == 0 && pipeline_worth_it(in, out_rows, H)) {
+        // Both operands and the output in host memory, rhs wide enough for four column blocks of
+        // at least 512: the 2-D schedule (8192^3: 7.42 ms against 7.84 in row blocks alone, same
+        // box and call).
+        const std::vector<long long> rows = block_bounds(H, 8, kPipeRowBlock, kPipeRowBlock);
+        const std::vector<long long> cols = block_bounds(W, kPipeMaxColBlocks, 64, 256);
+        DeviceInfo* dev = nullptr;
+        if ((rc = device_info(&dev)) != KG_OK) return rc;
+        bool ok = dev->num_sms >= 2;
+        for (size_t r = 0; ok && r + 1 < rows.size(); ++r)
+            for (size_t c = 0; ok && c + 1 < cols.size(); ++c)
+                ok = matmul_tile_ok(static_cast<float*>(out.dev) + static_cast<size_t>(rows[r]) * W + cols[c], W,
+                                    static_cast<const char*>(lhs.dev) + static_cast<size_t>(rows[r]) * K * 2,
+                                    static_cast<const char*>(rhs.dev) + static_cast<size_t>(cols[c]) * 2, W, rows[r + 1] - rows[r], K,
+                                    cols[c + 1] - cols[c]);
+        if (ok) return run_matmul_2d(out, lhs, rhs, bias, K, W, rows, cols);
+    }
     if (H >= 2 * kPipeRowBlock && pipeline_worth_it(in, out_rows, H)) {
         // 16 row blocks (the pipeline's maximum): the first download starts after a smaller
         // first block and the last block's download is a shorter tail (8192^3 from host buffers:
