@@ -864,9 +864,10 @@ int kg_sm100_matmul_entry(const KgArgSlot* slots, unsigned long long n) {
     if (lhs.dtype == KG_DTYPE_BF16 && rhs.host && (bias.data == nullptr || bias.host) && H >= 2 * kPipeRowBlock && W >= 2048 &&
         W % 8 == 0 && pipeline_worth_it(in, out_rows, H)) {
         // Both operands and the output in host memory, rhs wide enough for four column blocks of
-        // at least 512: the 2-D schedule (8192^3: 7.42 ms against 7.84 in row blocks alone, same
-        // box and call).
-        const std::vector<long long> rows = block_bounds(H, 8, kPipeRowBlock, kPipeRowBlock);
+        // at least 512: the 2-D schedule, 4 row blocks by 4 column blocks (8192^3: 7.42 ms against
+        // 7.84 in row blocks alone; 4 row blocks measured 7.52-7.53 against 7.64 for 8, 7.74 for
+        // 16 and 7.89 with 2 column blocks, on a slower box).
+        const std::vector<long long> rows = block_bounds(H, 4, kPipeRowBlock, kPipeRowBlock);
         const std::vector<long long> cols = block_bounds(W, kPipeMaxColBlocks, 64, 256);
         DeviceInfo* dev = nullptr;
         if ((rc = device_info(&dev)) != KG_OK) return rc;
