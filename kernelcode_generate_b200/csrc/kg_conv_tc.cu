@@ -333,16 +333,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 //  * Weight blocks (x >= x_blocks, y == 0): OIHW -> [F, KH*KW, Cp], zero in the channel padding;
 //    one thread per (f, c) reads the taps of weight[f, c] (contiguous) and writes one element per
 //    tap, neighbouring threads writing neighbouring c.
-// At most 40 registers per thread, so 6 blocks share an SM: the loads of 6 blocks are in flight at
-// once (4 blocks at 64 registers moved the X1 input at 3.1 TB/s, 6 at 3.4).
-constexpr int RP_PIX = 64, RP_CH = 64, RP_ROWS = 2;
+// Four padded rows per block, 8 loads of 16 bytes per thread in flight, 4 blocks per SM (X1 step
+// 126.0 vs 128.0 us with two rows and 6 blocks; 4 blocks of two rows moved the input at 3.1 TB/s).
+// The output mostly stays in L2 for the conv kernel that reads it next: per X1 launch 52.6 MB are
+// read from DRAM and 13.8 MB written in 32.6 us, so the repack is bound by latency, not DRAM.
+constexpr int RP_PIX = 64, RP_CH = 64, RP_ROWS = 4;
 constexpr int RP_TASKS = RP_ROWS * RP_CH * (RP_PIX / 8) / 256;  // 8-pixel loads per thread per chunk
 __device__ __forceinline__ int rp_col(int px, int c) { return c ^ (((px >> 3) & 7) << 3); }
 
 // PHASED: x_pad is stored as stride phase planes; SH/SW > 0 give the stride at compile time (the
 // per-store plane arithmetic then uses shifts), 0 reads it from the shape.
 template <bool PHASED, int SH = 0, int SW = 0>
-__global__ void __launch_bounds__(256, 6) conv_repack_kernel(__nv_bfloat16* __restrict__ x_pad, const __nv_bfloat16* __restrict__ src,
+__global__ void __launch_bounds__(256, 4) conv_repack_kernel(__nv_bfloat16* __restrict__ x_pad, const __nv_bfloat16* __restrict__ src,
                                                           __nv_bfloat16* __restrict__ w_ftc, const __nv_bfloat16* __restrict__ weight,
                                                           ConvTcShape s, int vec_ok, int x_blocks) {
     // The conv kernel launched after this one may start setting up now; it waits for this grid to
