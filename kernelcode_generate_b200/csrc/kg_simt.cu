@@ -154,14 +154,57 @@ __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ ou
     static_assert(W_PER * 256 == CV_BM * CV_BK && X_PER * 256 == CV_BK * CV_BN, "whole elements per thread");
     __shared__ float sw[CV_BK][CV_BM + 1];
     __shared__ float sx[CV_BK][CV_BN + 4];
+    // Index decompositions done once instead of per load (each needs integer divisions by runtime
+    // extents): per output column of the CTA the image's input offset, the top-left input position
+    // of its window and its output offset; per reduction position of the K step its channel's
+    // offset and its tap's offsets. A position outside the problem gets a top-left far out of range.
+    constexpr int FAR = -(1 << 29);
+    __shared__ long long c_in[CV_BN], c_out[CV_BN];
+    __shared__ int c_h0[CV_BN], c_w0[CV_BN];
+    __shared__ long long k_ch[CV_BK];
+    __shared__ int k_dh[CV_BK], k_dw[CV_BK];
     const int Kred = s.C * s.KH * s.KW;
     const long long Ncols = (long long)s.B * s.HO * s.WO;
+    const long long plane = (long long)s.XH * s.XW;
     const int f0 = blockIdx.y * CV_BM;
     const long long n0 = (long long)blockIdx.x * CV_BN;
     const int tx = threadIdx.x & 31;  // columns tx + 32 j
     const int ty = threadIdx.x >> 5;  // rows ty + 8 i
+    for (int c = threadIdx.x; c < CV_BN; c += 256) {
+        const long long col = n0 + c;
+        if (col < Ncols) {
+            const int b = (int)(col / ((long long)s.HO * s.WO));
+            const int sp = (int)(col - (long long)b * s.HO * s.WO);
+            const int ho = sp / s.WO, wo = sp - (sp / s.WO) * s.WO;
+            c_in[c] = (long long)b * s.C * plane;
+            c_out[c] = (long long)b * s.F * s.HO * s.WO + sp;
+            c_h0[c] = ho * s.sh - s.pt;
+            c_w0[c] = wo * s.sw - s.pl;
+        } else {
+            c_in[c] = 0;
+            c_out[c] = -1;
+            c_h0[c] = FAR;
+            c_w0[c] = FAR;
+        }
+    }
     float acc[TM][TN] = {};
     for (int k0 = 0; k0 < Kred; k0 += CV_BK) {
+        for (int r = threadIdx.x; r < CV_BK; r += 256) {
+            const int kk = k0 + r;
+            if (kk < Kred) {
+                const int ci = kk / (s.KH * s.KW);
+                const int rem = kk - ci * s.KH * s.KW;
+                const int khi = rem / s.KW;
+                k_ch[r] = (long long)ci * plane;
+                k_dh[r] = khi * s.dh;
+                k_dw[r] = (rem - khi * s.KW) * s.dw;
+            } else {
+                k_ch[r] = 0;
+                k_dh[r] = FAR;
+                k_dw[r] = FAR;
+            }
+        }
+        __syncthreads();
         // All of this step's loads are issued before any store, so their latencies overlap.
         float wv[W_PER], xv[X_PER];
 #pragma unroll
@@ -175,25 +218,9 @@ __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ ou
         for (int e = 0; e < X_PER; ++e) {
             const int i = threadIdx.x + 256 * e;
             const int r = i / CV_BN, c = i % CV_BN;
-            const int kk = k0 + r;
-            const long long col = n0 + c;
-            float v = 0.0f;
-            if (kk < Kred && col < Ncols) {
-                const int ci = kk / (s.KH * s.KW);
-                const int rem = kk - ci * s.KH * s.KW;
-                const int khi = rem / s.KW;
-                const int kwi = rem - khi * s.KW;
-                const int b = (int)(col / ((long long)s.HO * s.WO));
-                const int sp = (int)(col - (long long)b * s.HO * s.WO);
-                const int ho = sp / s.WO;
-                const int wo = sp - ho * s.WO;
-                const int h = ho * s.sh - s.pt + khi * s.dh;
-                const int w = wo * s.sw - s.pl + kwi * s.dw;
-                if (h >= 0 && h < s.XH && w >= 0 && w < s.XW) {
-                    v = to_f32(input[(((size_t)b * s.C + ci) * s.XH + h) * s.XW + w]);
-                }
-            }
-            xv[e] = v;
+            const int h = c_h0[c] + k_dh[r];
+            const int w = c_w0[c] + k_dw[r];
+            xv[e] = (h >= 0 && h < s.XH && w >= 0 && w < s.XW) ? to_f32(input[c_in[c] + k_ch[r] + (long long)h * s.XW + w]) : 0.0f;
         }
 #pragma unroll
         for (int e = 0; e < W_PER; ++e) {
@@ -226,11 +253,9 @@ __global__ void __launch_bounds__(256) conv2d_simt_kernel(float* __restrict__ ou
         if (f >= s.F) continue;
 #pragma unroll
         for (int j = 0; j < TN; ++j) {
-            const long long col = n0 + tx + 32 * j;
-            if (col >= Ncols) continue;
-            const int b = (int)(col / ((long long)s.HO * s.WO));
-            const int sp = (int)(col - (long long)b * s.HO * s.WO);
-            out[((size_t)b * s.F + f) * s.HO * s.WO + sp] = acc[i][j] + (bias ? bias[f] : 0.0f);
+            const long long o = c_out[tx + 32 * j];
+            if (o < 0) continue;
+            out[o + (long long)f * s.HO * s.WO] = acc[i][j] + (bias ? bias[f] : 0.0f);
         }
     }
 }
