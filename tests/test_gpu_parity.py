@@ -300,12 +300,13 @@ def test_host_buffer_matmul_row_blocks_match_device_path(cuda_device, M, with_bi
     np.testing.assert_allclose(host_out.numpy(), expect, **BF16_TOL)
 
 
-@pytest.mark.parametrize("M,K,N,with_bias", [(3000, 1024, 3000, True), (4100, 2048, 1304, False), (2600, 512, 4096, True)])
+@pytest.mark.parametrize("M,K,N,with_bias", [(3000, 1024, 3000, True), (4100, 2048, 1304, False), (2600, 512, 4096, True),
+                                             (4000, 512, 2056, True)])
 def test_host_buffer_matmul_large_row_blocks_match_device_path(cuda_device, M, K, N, with_bias):
-    """Host lhs, rhs and out of 32 MiB and more. N >= 2048: the 2-D schedule (row blocks of lhs by
-    four column blocks of rhs, ragged last blocks, pitched tile launches and 2-D copies); N = 1304:
-    row blocks of 512 with a ragged last block. The result equals the one-launch device-buffer
-    result bit for bit."""
+    """Host lhs, rhs and out of 32 MiB and more. N >= 2048: the 2-D schedule (four row blocks of lhs
+    by four column blocks of rhs, ragged last blocks such as 328 columns of 2056, pitched tile
+    launches and 2-D copies); N = 1304: row blocks of 512 with a ragged last block. The result
+    equals the one-launch device-buffer result bit for bit."""
     torch = _torch()
     rng = np.random.default_rng(M + N)
     a = workloads.bf16_bits(rng.standard_normal((M, K), dtype=np.float32))
