@@ -319,7 +319,12 @@ struct FaCfg {
     static constexpr int LDK = BC + 4;      // row pitch of the transposed K tile
     static constexpr int LDV = DP + 4;
     static constexpr int LDP = BR + 4;      // row pitch of the transposed P tile ([key][row])
-    static constexpr size_t floats = (size_t)DP * LDQ + (size_t)DP * LDK + (size_t)BC * LDV + (size_t)BC * LDP + 2 * BR;
+    // With 8 keys per thread (KQ = 2) P is stored over the K tile, which QK^T no longer reads once
+    // the scores are in registers: 87.5 KB instead of 121 KB at D = 64, so two CTAs fit on an SM.
+    static constexpr bool P_OVER_K = KQ > 1;
+    static constexpr size_t K_REGION = P_OVER_K ? ((size_t)DP * LDK > (size_t)BC * LDP ? (size_t)DP * LDK : (size_t)BC * LDP)
+                                                : (size_t)DP * LDK;
+    static constexpr size_t floats = (size_t)DP * LDQ + K_REGION + (size_t)BC * LDV + (P_OVER_K ? 0 : (size_t)BC * LDP) + 2 * BR;
     // Output columns a thread owns: with DT % 4 == 0, DT / 4 groups of 4 contiguous columns
     // (64 g + 4 tx .. + 3), so each P.V step reads them as float4s; otherwise tx + 16 c.
     static constexpr bool VEC_COLS = DT % 4 == 0;
@@ -363,9 +368,10 @@ __global__ void __launch_bounds__(256, FaCfg<DT, RA, KQ>::MIN_BLOCKS)
     float* fa_smem = reinterpret_cast<float*>(fa_smem4);
     float* sQt = fa_smem;                // [DP][LDQ]
     float* sKt = sQt + DP * LDQ;         // [DP][LDK]
-    float* sV = sKt + DP * LDK;          // [BC][LDV]; after the key loop, a split's partial O [BR][DP]
-    float* sP = sV + BC * LDV;           // [BC][LDP]: P transposed, a thread's RA rows contiguous
-    float* sM = sP + BC * LDP;           // [BR]: a split's running max per row
+    float* sV = sKt + L::K_REGION;       // [BC][LDV]; after the key loop, a split's partial O [BR][DP]
+    // [BC][LDP]: P transposed, a thread's RA rows contiguous (over the K tile when P_OVER_K)
+    float* sP = L::P_OVER_K ? sKt : sV + BC * LDV;
+    float* sM = sV + BC * LDV + (L::P_OVER_K ? 0 : BC * LDP);  // [BR]: a split's running max per row
     float* sL = sM + BR;                 // [BR]: a split's running sum per row
     cg::cluster_group cluster = cg::this_cluster();
     const int ns = static_cast<int>(cluster.num_blocks());
@@ -552,6 +558,7 @@ __global__ void __launch_bounds__(256, FaCfg<DT, RA, KQ>::MIN_BLOCKS)
             m_run[a] = m_new;
         }
         // P transposed: key 64q + 4tx + b, this thread's RA consecutive rows as vector stores.
+        if constexpr (L::P_OVER_K) __syncthreads();  // every warp is done reading the K tile
 #pragma unroll
         for (int t = 0; t < NK; ++t) {
             float col_p[RA];
@@ -721,11 +728,15 @@ static cudaError_t flash_attn_simt_launch_ra(T* out, const T* q, const T* k, con
     return cudaLaunchKernelEx(&cfg, kernel, out, q, k, v, H, S, D, scale_log2, causal, key_split);
 }
 
-// Register tiles served: rows x keys per thread 1x4, 2x4 and 4x4. (An 8 x 8 tile, 128 x 128 per
-// CTA and one CTA per SM, measured no faster on C3: 32.8 vs 32.8 us with a 4-way split.)
+// Register tiles served: rows x keys per thread 1x4, 2x4, 4x4 and 4x8. (An 8 x 8 tile, 128 x 128
+// per CTA and one CTA per SM, measured no faster on C3: 32.8 vs 32.8 us with a 4-way split; 8 x 4
+// spilled at two CTAs per SM and measured 35.2-36.7 us.)
 template <typename T, int DT>
 static cudaError_t flash_attn_simt_launch_dt(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
-                                             int ra, int ns, cudaStream_t stream) {
+                                             int ra, int kq, int ns, cudaStream_t stream) {
+    if (kq == 2) return ra == 4 ? flash_attn_simt_launch_ra<T, DT, 4, 2>(out, q, k, v, B, H, S, D, scale, causal, ns, stream)
+                                : cudaErrorInvalidValue;
+    if (kq != 1) return cudaErrorInvalidValue;
     switch (ra) {
         case 4: return flash_attn_simt_launch_ra<T, DT, 4, 1>(out, q, k, v, B, H, S, D, scale, causal, ns, stream);
         case 2: return flash_attn_simt_launch_ra<T, DT, 2, 1>(out, q, k, v, B, H, S, D, scale, causal, ns, stream);
@@ -736,46 +747,53 @@ static cudaError_t flash_attn_simt_launch_dt(T* out, const T* q, const T* k, con
 
 template <typename T>
 cudaError_t flash_attn_simt_launch_cfg(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
-                                       int ra, int ns, cudaStream_t stream) {
+                                       int ra, int kq, int ns, cudaStream_t stream) {
     if (!(ns == 1 || ns == 2 || ns == 4 || ns == 8)) return cudaErrorInvalidValue;
     switch ((D + 15) / 16) {
-        case 1: return flash_attn_simt_launch_dt<T, 1>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
-        case 2: return flash_attn_simt_launch_dt<T, 2>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
-        case 3: return flash_attn_simt_launch_dt<T, 3>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
-        case 4: return flash_attn_simt_launch_dt<T, 4>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
-        case 5: return flash_attn_simt_launch_dt<T, 5>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
-        case 6: return flash_attn_simt_launch_dt<T, 6>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
-        case 7: return flash_attn_simt_launch_dt<T, 7>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
-        case 8: return flash_attn_simt_launch_dt<T, 8>(out, q, k, v, B, H, S, D, scale, causal, ra, ns, stream);
+        case 1: return flash_attn_simt_launch_dt<T, 1>(out, q, k, v, B, H, S, D, scale, causal, ra, kq, ns, stream);
+        case 2: return flash_attn_simt_launch_dt<T, 2>(out, q, k, v, B, H, S, D, scale, causal, ra, kq, ns, stream);
+        case 3: return flash_attn_simt_launch_dt<T, 3>(out, q, k, v, B, H, S, D, scale, causal, ra, kq, ns, stream);
+        case 4: return flash_attn_simt_launch_dt<T, 4>(out, q, k, v, B, H, S, D, scale, causal, ra, kq, ns, stream);
+        case 5: return flash_attn_simt_launch_dt<T, 5>(out, q, k, v, B, H, S, D, scale, causal, ra, kq, ns, stream);
+        case 6: return flash_attn_simt_launch_dt<T, 6>(out, q, k, v, B, H, S, D, scale, causal, ra, kq, ns, stream);
+        case 7: return flash_attn_simt_launch_dt<T, 7>(out, q, k, v, B, H, S, D, scale, causal, ra, kq, ns, stream);
+        case 8: return flash_attn_simt_launch_dt<T, 8>(out, q, k, v, B, H, S, D, scale, causal, ra, kq, ns, stream);
         default: return cudaErrorInvalidValue;
     }
 }
 
-FlashSimtConfig flash_attn_simt_config(int B, int H, int S, int causal) {
+FlashSimtConfig flash_attn_simt_config(int B, int H, int S, int D, int causal, bool f32) {
     // 64-row query tiles (4 rows per thread: 16 FMAs per pair of 16-byte shared loads) unless the
     // sequence is short enough that most of such a tile would be padding. Then the keys of each
     // query tile are split over 2, 4 or 8 CTAs of a cluster until the grid holds 1.5 CTAs per SM
     // (3 for causal, whose early query tiles see few keys and whose empty splits end at once).
     // Measured on B200, fp32, L2 flushed (us): 1x8x512x64 rows/thread x split 4x4 32.8 (2x1 47.1,
     // 4x8 37.9); 1x4x300x40 causal 4x8 18.5 (2x1 26.6); 2x3x1000x64 causal 4x8 81.1 (2x1 113.0).
-    FlashSimtConfig c{S > 32 ? 4 : (S > 16 ? 2 : 1), 1};
+    FlashSimtConfig c{S > 32 ? 4 : (S > 16 ? 2 : 1), 1, 1};
     const long long tiles = static_cast<long long>((S + 16 * c.ra - 1) / (16 * c.ra)) * B * H;
     const long long want = 148LL * 3 / 2;
     while (c.ns < 8 && tiles * c.ns < want * (causal ? 2 : 1)) c.ns *= 2;
+    // 8 keys per thread (128-key tiles, P stored over the K tile) when every split holds at least
+    // one full 128-key tile: three 16-byte shared loads per 32 FMAs in Q.K^T instead of two per 16,
+    // and one tile load round trip instead of two where a split holds 128 keys. fp32 with D <= 64
+    // only (larger D, or bf16 planes, spill at the 128-register cap). Measured (us, L2 flushed):
+    // 1x8x512x64 split 4: 30.7 vs 32.8; 2x8x1024x64 unsplit: 157 vs 173; causal shapes level
+    // (1x4x300x40 18.5 vs 18.3, 2x3x1000x64 80.3 vs 80.9), so they keep 4 keys per thread.
+    if (f32 && !causal && D <= 64 && c.ra == 4 && S / c.ns >= 128) c.kq = 2;
     return c;
 }
 
 template <typename T>
 cudaError_t flash_attn_simt_launch(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
                                    cudaStream_t stream) {
-    const FlashSimtConfig c = flash_attn_simt_config(B, H, S, causal);
-    return flash_attn_simt_launch_cfg(out, q, k, v, B, H, S, D, scale, causal, c.ra, c.ns, stream);
+    const FlashSimtConfig c = flash_attn_simt_config(B, H, S, D, causal, sizeof(T) == 4);
+    return flash_attn_simt_launch_cfg(out, q, k, v, B, H, S, D, scale, causal, c.ra, c.kq, c.ns, stream);
 }
 template cudaError_t flash_attn_simt_launch<float>(float*, const float*, const float*, const float*, int, int, int, int, float, int,
                                                    cudaStream_t);
 template cudaError_t flash_attn_simt_launch<__nv_bfloat16>(__nv_bfloat16*, const __nv_bfloat16*, const __nv_bfloat16*,
                                                            const __nv_bfloat16*, int, int, int, int, float, int, cudaStream_t);
 template cudaError_t flash_attn_simt_launch_cfg<float>(float*, const float*, const float*, const float*, int, int, int, int, float, int, int,
-                                                       int, cudaStream_t);
+                                                       int, int, cudaStream_t);
 
 }  // namespace kg

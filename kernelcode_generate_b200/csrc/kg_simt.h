@@ -22,15 +22,17 @@ template <typename T>
 cudaError_t flash_attn_simt_launch(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
                                    cudaStream_t stream);
 
-// Launch shape of the CUDA-core attention kernel: `ra` query rows per thread (16 * ra per CTA) and
-// `ns` CTAs per thread-block cluster sharing each query tile's keys (1, 2, 4 or 8).
+// Launch shape of the CUDA-core attention kernel: `ra` query rows per thread (16 * ra per CTA),
+// `kq` groups of 4 keys per thread (64 * kq keys per tile; kq = 2 only with ra = 4) and `ns` CTAs
+// per thread-block cluster sharing each query tile's keys (1, 2, 4 or 8).
 struct FlashSimtConfig {
     int ra;
     int ns;
+    int kq;
 };
-FlashSimtConfig flash_attn_simt_config(int B, int H, int S, int causal);
+FlashSimtConfig flash_attn_simt_config(int B, int H, int S, int D, int causal, bool f32);
 template <typename T>
 cudaError_t flash_attn_simt_launch_cfg(T* out, const T* q, const T* k, const T* v, int B, int H, int S, int D, float scale, int causal,
-                                       int ra, int ns, cudaStream_t stream);
+                                       int ra, int kq, int ns, cudaStream_t stream);
 
 }  // namespace kg

@@ -401,7 +401,12 @@ def test_f32_flash_attention_cuda_cores_many_heads(cuda_device):
     np.testing.assert_allclose(out.cpu().numpy(), expect, **FP32_TOL)
 
 
-@pytest.mark.parametrize("S,D,causal", [(200, 16, False), (130, 40, True), (257, 64, True), (96, 100, False), (333, 128, True)])
+# (1300, 40) and (1100, 30), non-causal, take 8 keys per thread (128-key tiles, P stored over the
+# K tile): 1300 splits 4 ways into 384-key ranges (three tiles per CTA; the last range holds 148
+# keys, a full tile and a 20-key tail); 1100 splits 8 ways into four 256-key ranges, a 76-key one
+# and three empty ones, on the scalar tile loads (D % 4 != 0).
+@pytest.mark.parametrize("S,D,causal", [(200, 16, False), (130, 40, True), (257, 64, True), (96, 100, False), (333, 128, True),
+                                        (1300, 40, False), (1100, 30, False)])
 def test_f32_flash_attention_cuda_cores_vs_oracle(cuda_device, S, D, causal):
     """fp32 attention on the CUDA-core kernel, one head-dim width per case (16 columns per thread
     group), sequence tails inside a 64-row block, within the fp32 tolerance."""
